@@ -1,0 +1,318 @@
+"""Benchmark of the krunch compress hot path.
+
+Workload (per GPU): RWKV-4-169M (12 x 768, FFN 3072, vocab 50277), fp16
+random-init weights (seed 0); B = 64 chunks x T = 4096 token ids drawn
+i.i.d. Zipf(1.1) over the vocabulary through a seeded permutation (seed =
+rank); full packed forward, head logits, 16-bit CDF, GPU range encode.  One
+step = compressing that whole batch.  Synthetic data: no corpus, tokenizer
+file or pretrained weights exist in this environment.
+
+value : MB/s of input with the inputs resident in HBM (bytes = tokens x
+        bytes_per_token, 1 byte per token: the byte-level tokenizer this build
+        ships); whole job over all ranks, time = max over ranks (CUDA events).
+e2e   : the same through the public API (Codec.compress_tokens): token ids
+        from pinned host memory in, bitstreams back to the host, per step.
+roofline : the dominant kernel family (the layer GEMMs), FLOPs / event time.
+cpu_baseline : the CPU oracle port (numpy fp32 forward + C CDF + C coder)
+        on a bounded sample, rank 0 at N = 1.
+
+--impl reference runs that CPU port (the reference's own path is Python +
+CUDA that needs the absent `rwkv` package, so its CPU restatement stands in)
+on rank 0 with all host threads.
+
+Multi-GPU: one process per GPU (torchrun); each rank compresses its own 64
+chunks (weak scaling, no data-path collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "compress MB/s of input (RWKV-4-169M, 16-bit CDF, byte-exact)"
+BYTES_PER_TOKEN = 1.0
+SHAPE = dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = [r.split(",") for r in Path(self.f.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if "Active" in v
+                          and "Not" not in v})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_port_compress(n_chunks: int, n_tok: int, bits: int, threads: int):
+    """The CPU oracle pipeline on n_chunks x n_tok Zipf tokens; returns (seconds, tokens)."""
+    import torch  # noqa: F401  (numpy BLAS threads follow the process env)
+    from krunch_b200.synth import random_weights, zipf_tokens
+    from oracle import coder, rwkv
+    w = random_weights(**SHAPE, seed=0)
+    toks = zipf_tokens((n_chunks, n_tok), seed=0)
+    inp = np.concatenate([np.zeros((n_chunks, 1), np.int32), toks[:, :-1]], axis=1)
+    t0 = time.perf_counter()
+    lg, _ = rwkv.forward(w, inp)
+    lh = coder.lohi_from_logits(lg.reshape(-1, lg.shape[-1]).astype(np.float16),
+                                toks.reshape(-1), bits, threads=threads)
+    lh = lh.reshape(n_chunks, n_tok, 2)
+    total = sum(len(coder.encode_lohi(lh[b], bits)) for b in range(n_chunks))
+    dt = time.perf_counter() - t0
+    return dt, n_chunks * n_tok, total
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        cpu_port_compress(1, 16, args.cdf_bits, threads)
+    times, toks = [], 0
+    for _ in range(args.steps):
+        dt, n, _ = cpu_port_compress(args.ref_chunks, args.ref_tokens, args.cdf_bits, threads)
+        times.append(dt)
+        toks = n
+    sec = float(np.mean(times))
+    v = toks * BYTES_PER_TOKEN / sec / 1e6
+    sample = f"{args.ref_chunks} chunks x {args.ref_tokens} tokens of the config workload per step"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "MB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config(args),
+        "cpu_baseline": {"value": v, "unit": "MB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "MB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def config(args):
+    return {"workload": "configs[1] compress, packed forward, 1 GPU per rank",
+            "model": "RWKV-4-169M random-init fp16", "chunks_per_gpu": args.B,
+            "tokens_per_chunk": args.T, "cdf_bits": args.cdf_bits,
+            "bytes_per_token": BYTES_PER_TOKEN, "token_dist": "Zipf(1.1) via seeded permutation",
+            "global_batch": args.B * args.gpus, "seq_len": args.T,
+            "parallelism": f"chunk-replica x{args.gpus}",
+            "l2": "inputs larger than L2 (fp16 logits window >> 126 MB)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--B", type=int, default=64)
+    ap.add_argument("--T", type=int, default=4096)
+    ap.add_argument("--cdf-bits", type=int, default=16)
+    ap.add_argument("--ref-chunks", type=int, default=4)
+    ap.add_argument("--ref-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decompress", action="store_true",
+                    help="also time configs[2]-shaped decompress (fp16 weights)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from krunch_b200 import _native as N
+    from krunch_b200 import distributed as kd
+    from krunch_b200.codec import Codec, CompressPlan
+    from krunch_b200.model import RWKVModel
+    from krunch_b200.synth import random_weights, zipf_tokens
+
+    kd.init_from_env()
+    rank, world = kd.rank(), kd.world()
+    args.gpus = world
+    dev = torch.device("cuda", kd.local_rank() % torch.cuda.device_count())
+    torch.cuda.set_device(dev)
+    w = random_weights(**SHAPE, seed=0)
+    model = RWKVModel(w, device=dev)
+    del w
+    codec = Codec(model, cdf_bits=args.cdf_bits)
+    toks = zipf_tokens((args.B, args.T), seed=rank)
+    seqs = list(toks)
+    plan = CompressPlan(codec, [args.T] * args.B)
+    plan.upload(seqs)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing ------------------------------------------
+    for _ in range(args.warmup):
+        plan.run()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        N.profile_begin()
+        e0.record(stream)
+        for _ in range(args.steps):
+            plan.run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        prof = N.profile_end()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    streams = plan.fetch()
+    comp_bytes = sum(len(s) for s in streams)
+    tokens_all = args.B * args.T * world
+    value = tokens_all * BYTES_PER_TOKEN / (ms / 1e3) / 1e6
+    launches = int(sum(v[1] for v in prof.values())) // args.steps
+
+    # ---- roofline of the dominant kernel family -----------------------------
+    pk, pk_kind = peaks()
+    dom = max(("gemm", "head", "cdf", "wkv", "ln_mix"), key=lambda k: prof[k][0])
+    kern = {}
+    for k, (kms, n, work) in prof.items():
+        if n == 0:
+            continue
+        if k in ("gemm", "head"):
+            ach = work / (kms / 1e3) / 1e12
+            kern[k] = {"ms_per_step": kms / args.steps, "launches_per_step": n // args.steps,
+                       "achieved": ach, "unit": "TFLOP/s",
+                       "frac": ach / pk["bf16_tflops_sustained"]}
+        else:
+            ach = work / (kms / 1e3) / 1e9
+            kern[k] = {"ms_per_step": kms / args.steps, "launches_per_step": n // args.steps,
+                       "achieved": ach, "unit": "GB/s", "frac": ach / pk["hbm_gbs"]}
+    d = kern[dom]
+    roofline = {"kernel": dom, "bound": "tensor" if d["unit"] == "TFLOP/s" else "hbm",
+                "achieved": d["achieved"], "unit": d["unit"],
+                "peak": pk["bf16_tflops_sustained"] if d["unit"] == "TFLOP/s" else pk["hbm_gbs"],
+                "peak_kind": f"{pk_kind} (bf16 sustained / HBM copy)", "frac": d["frac"],
+                "traffic": None, "per_family": kern}
+
+    # ---- end-to-end through the public API ---------------------------------
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(max(1, args.steps)):
+        p2 = CompressPlan(codec, [args.T] * args.B)
+        p2.upload(seqs)
+        p2.run()
+        out2 = p2.fetch()
+    e3.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e2.elapsed_time(e3) / max(1, args.steps))
+    wall_ms = (time.perf_counter() - t0) * 1e3 / max(1, args.steps)
+    assert out2 == streams, "compress is not deterministic across runs"
+    e2e = {"value": tokens_all * BYTES_PER_TOKEN / (e2e_ms / 1e3) / 1e6, "unit": "MB/s",
+           "h2d_bytes_per_step": p2.h2d_bytes, "d2h_bytes_per_step": p2.d2h_bytes,
+           "wall_ms_per_step": wall_ms}
+
+    extra = {}
+    if args.decompress:
+        from krunch_b200.codec import DecompressPlan
+        Bd, Td = 256, 2048
+        dseqs = list(zipf_tokens((Bd, Td), seed=100 + rank))
+        dstreams = codec.compress_tokens(dseqs)
+        dp = DecompressPlan(codec, [len(s) for s in dstreams], [Td] * Bd)
+        dp.upload(dstreams)
+        dp.run()  # warm-up + graph capture
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        dp.run()
+        d1.record(stream)
+        torch.cuda.synchronize()
+        dms = max_over_ranks(d0.elapsed_time(d1))
+        ok = all(np.array_equal(a, b) for a, b in zip(dp.fetch(), dseqs))
+        extra["decompress"] = {
+            "workload": "configs[2] shape (B=256 x 2048 steps), fp16 weights (int8 not built)",
+            "value": Bd * Td * world * BYTES_PER_TOKEN / (dms / 1e3) / 1e6, "unit": "MB/s",
+            "us_per_step": dms * 1e3 / Td, "byte_exact": ok}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        dt, n, _ = cpu_port_compress(args.ref_chunks, args.ref_tokens, args.cdf_bits, threads)
+        cpu = {"value": n * BYTES_PER_TOKEN / dt / 1e6, "unit": "MB/s", "cores": threads,
+               "kind": "port",
+               "sample": f"{args.ref_chunks} chunks x {args.ref_tokens} tokens, {dt:.1f} s"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "MB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (Zipf token ids, random-init weights)",
+                "config": config(args), "tokens_per_s": tokens_all / (ms / 1e3),
+                "bits_per_token": 8.0 * comp_bytes / (args.B * args.T),
+                "gpu_launches": launches, "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "clocks": clk.summary(), **extra}
+        print(json.dumps(line))
+    kd.shutdown()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,245 @@
+/*
+ * krunch_b200 — C ABI of the B200-native krunch compress/decompress hot path.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and an explicit
+ * cudaStream_t (passed as void* so this header needs no CUDA include), enqueues
+ * work on that stream and returns without synchronising.  Return value is a
+ * kb_status (0 = ok, negative = error).  On KB_ERR_CUDA the CUDA error code is
+ * kept in a thread-local slot readable with kb_last_cuda_error().
+ *
+ * Hot-path calls never allocate device memory: callers size a workspace with
+ * the matching *_workspace_bytes() query and pass it in.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths are relative to the dmatth1/krunch source tree).
+ */
+#ifndef KRUNCH_B200_H
+#define KRUNCH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------- */
+/* status                                                                    */
+/* ------------------------------------------------------------------------- */
+enum kb_status {
+    KB_OK = 0,
+    KB_ERR_ARG = -1,         /* null pointer / bad enum / bad size            */
+    KB_ERR_SHAPE = -2,       /* unsupported shape (e.g. K not multiple of 64) */
+    KB_ERR_ALIGN = -3,       /* pointer or stride not aligned as required     */
+    KB_ERR_CUDA = -4,        /* CUDA runtime error, see kb_last_cuda_error()  */
+    KB_ERR_TIMEOUT = -5,     /* bounded device wait expired                   */
+    KB_ERR_UNSUPPORTED = -6, /* feature not built for this device             */
+    KB_ERR_WORKSPACE = -7,   /* workspace smaller than the query returned     */
+    KB_ERR_NOMEM = -8        /* host allocation failed (model handle)         */
+};
+
+const char* kb_version(void);
+
+/* Phase profiler (the counterpart of the reference's KRUNCH_PHASE_PROFILE
+ * event timers, krunch_ac/cuda/layer_cpp.cpp:111-157, read_phase_times
+ * 825-836).  Between begin and end every launch of this library is bracketed
+ * by CUDA events on its stream.  end() waits for those events and fills, per
+ * phase (0 embed, 1 layernorm+mix, 2 layer GEMMs, 3 WKV, 4 head GEMM,
+ * 5 CDF, 6 encode, 7 decode step), the summed milliseconds, the launch count
+ * and the algorithmic work (FLOPs for GEMM phases, bytes otherwise).
+ * Host-thread global; not for use inside stream capture. */
+int kb_profile_begin(void);
+int kb_profile_end(double* ms, int64_t* launches, double* work, int n_phases);
+const char* kb_status_string(int status);
+int kb_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------- */
+/* range coder — one lane (thread) per stream                                */
+/*                                                                           */
+/* Per-stream state is 4 x uint32:                                           */
+/*   encoder {low, high, pending, bit_offset}                                */
+/*   decoder {low, high, value,   bit_offset}                                */
+/* Same layout as RangeState / DecodeState in                                */
+/* krunch_ac/cuda/range_coder.cuh:24-40.  cdf_bits is the log2 of the CDF     */
+/* total (16 or 24; the reference hard-codes 24, range_coder.cuh:19).         */
+/* Output bits are MSB-first; output buffers must be zeroed beyond the        */
+/* current bit_offset (krunch_ac/cpu_reference.py:91-147 bit order).          */
+/* Stream b writes/reads bytes starting at base + offsets[b] (offsets NULL    */
+/* means every stream starts at byte 0, used with B == 1).  out_bytes /       */
+/* in_bytes bound the whole buffer: writes past it are dropped (bit_offset    */
+/* still advances, so the host detects overflow) and reads past it return     */
+/* zero bits, the CPU reference's past-EOF rule (cpu_reference.py:68-72).     */
+/* ------------------------------------------------------------------------- */
+
+/* low=0, high=0xFFFFFFFF, pending=0, bit_offset=0 for n streams
+ * (replaces the host-side state init in krunch/inference.py:325-330). */
+int kb_coder_encode_init(uint32_t* states, int n_streams, void* stream);
+
+/* Encode n rows of one stream from full CDF rows:
+ * cdf int32 [n, cdf_stride] (cdf[i,0]=0, cdf[i,V]=2^cdf_bits), symbols int32 [n].
+ * Replaces encode_step (krunch_ac/cuda/main.cpp:114-143,
+ * encode_kernel.cu:53-103). */
+int kb_coder_encode_cdf(const int32_t* cdf, int64_t cdf_stride, const int32_t* symbols,
+                        int n, int cdf_bits, uint8_t* out, int64_t out_bytes,
+                        uint32_t* state, void* stream);
+
+/* One symbol per stream for B streams: cdfs int32 [B, cdf_stride].
+ * Replaces encode_step_batched (main.cpp:254-284, encode_kernel.cu:148-197). */
+int kb_coder_encode_cdf_batched(const int32_t* cdfs, int64_t cdf_stride,
+                                const int32_t* symbols, int B, int cdf_bits,
+                                uint8_t* out, int64_t out_bytes, const int64_t* out_offsets,
+                                uint32_t* states, void* stream);
+
+/* Lane-per-stream encode of pre-narrowed intervals: lohi uint32 [B, T, 2]
+ * holds (cdf[sym], cdf[sym+1]) for every row (written by kb_cdf_rows in
+ * KB_CDF_LOHI mode); stream b encodes rows 0..n_valid[b]-1 (n_valid NULL =
+ * all T).  This is the fused replacement of the per-chunk serial
+ * encode_step<<<1,1>>> loop (krunch/inference.py:331-338). */
+int kb_coder_encode_lohi(const uint32_t* lohi, int B, int T, const int32_t* n_valid,
+                         int cdf_bits, uint8_t* out, int64_t out_bytes,
+                         const int64_t* out_offsets, uint32_t* states, void* stream);
+
+/* Final flush: one bit + pending bits.  Replaces encode_finalize /
+ * encode_finalize_batched (encode_kernel.cu:106-119, main.cpp:145-156,286-303). */
+int kb_coder_encode_finalize(uint8_t* out, int64_t out_bytes, const int64_t* out_offsets,
+                             uint32_t* states, int B, void* stream);
+
+/* Read the first 32 bits of each stream.  Replaces decode_init /
+ * decode_init_batched (decode_kernel.cu:28-45,138-160; main.cpp:158-219). */
+int kb_coder_decode_init(const uint8_t* in, int64_t in_bytes, const int64_t* in_offsets,
+                         uint32_t* states, int B, void* stream);
+
+/* Decode one symbol per stream from full CDF rows cdfs int32 [B, cdf_stride]
+ * with V = number of symbols.  Replaces decode_step / decode_step_batched
+ * (decode_kernel.cu:49-110,162-216; main.cpp:173-252). */
+int kb_coder_decode_cdf(const int32_t* cdfs, int64_t cdf_stride, int V, int cdf_bits,
+                        const uint8_t* in, int64_t in_bytes, const int64_t* in_offsets,
+                        uint32_t* states, int32_t* out_syms, int B, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* logits -> softmax -> integer CDF (one CTA per row, row-local, bit-identical */
+/* for any number of rows).  Spec: krunch_ac/cdf.py:22-74 (count =            */
+/* floor(p*(T-V))+1, deficit to argmax with smallest-index tie-break) and     */
+/* krunch_ac/cuda/det_softmax_cdf.cu:62-185.                                  */
+/* ------------------------------------------------------------------------- */
+enum kb_cdf_mode {
+    KB_CDF_COUNTS = 0, /* out int32 [rows, V+1]: 0, count_0 .. count_{V-1}
+                          (det_softmax_cdf contract, layer_cpp.cpp:1041-1052) */
+    KB_CDF_CDF = 1,    /* out int32 [rows, V+1]: cumulative CDF            */
+    KB_CDF_LOHI = 2    /* out uint32 [rows, 2]: (cdf[s], cdf[s+1]) for
+                          s = symbols[row]; feeds kb_coder_encode_lohi      */
+};
+
+/* logits fp16 [rows, row_stride] (V valid columns). */
+int kb_cdf_rows(const uint16_t* logits_f16, int64_t row_stride, int rows, int V,
+                int cdf_bits, int mode, const int32_t* symbols, void* out, void* stream);
+
+/* probs fp32 [rows, V] -> int32 CDF [rows, V+1].  Replaces probs_to_cdf_gpu
+ * (krunch_ac/gpu_encode.py:22-48) with a fixed-order row reduction. */
+int kb_cdf_from_probs(const float* probs, int rows, int V, int cdf_bits, int32_t* cdf_out,
+                      void* stream);
+
+/* Fused decompress step tail: for each of B streams, softmax->CDF of its
+ * logits row, target search and range-decoder update, one CTA per stream.
+ * Replaces softmax_cdfs_per_row + decode_step_batched
+ * (krunch/cpp_path.py:490-512, krunch/inference.py:426-434).
+ * counters int32 [B, 2] = {symbols decoded so far, symbols in the stream}
+ * (NULL: every stream active).  A finished stream keeps its state and gets
+ * symbol 0 (the BOS pad input).  The decoded symbol goes to out_syms[b] (the
+ * next step's input token) and, when history is non-NULL, to
+ * history[b * hist_stride + counters[b][0]].  All pointers stay fixed from
+ * step to step, so a decode step can be captured in a CUDA graph. */
+int kb_decode_logits_step(const uint16_t* logits_f16, int64_t row_stride, int B, int V,
+                          int cdf_bits, const uint8_t* in, int64_t in_bytes,
+                          const int64_t* in_offsets, uint32_t* states, int32_t* counters,
+                          int32_t* out_syms, int32_t* history, int64_t hist_stride,
+                          void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* GEMM: out[M,N] = epilogue(A[M,K] @ W^T) with W stored K-major as [N,K]    */
+/* (the transpose of the reference's [in,out] layout).  One tile schedule and */
+/* one K order for every M, so each output row is bit-identical whatever M is */
+/* (the M-invariance contract of krunch_ac/cuda/det_matmul_tc*.cu).           */
+/* Replaces det_matmul (layer_cpp.cpp:728-822) and gemm_fp16 (206-290).       */
+/* ------------------------------------------------------------------------- */
+enum kb_epilogue {
+    KB_EPI_F32 = 0,        /* out fp32 = acc                                 */
+    KB_EPI_F16 = 1,        /* out fp16 = acc                                 */
+    KB_EPI_SIGMOID = 2,    /* out fp16 = sigmoid(acc)                        */
+    KB_EPI_RELU_SQ = 3,    /* out fp16 = relu(acc)^2                         */
+    KB_EPI_RESID = 4,      /* out fp16 = resid + acc                         */
+    KB_EPI_GATE_RESID = 5  /* out fp16 = resid + gate * acc                  */
+};
+enum kb_dtype { KB_F16 = 0, KB_BF16 = 1, KB_I8 = 2 };
+
+/* A, W: fp16 (dtype KB_F16).  resid/gate fp16 [M, ldo] (may alias out).
+ * Requires N % 128 == 0, K % 64 == 0, 16-byte aligned rows. */
+int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
+            int M, int N, int K, int epilogue, void* out, int64_t ldo,
+            const uint16_t* resid, const uint16_t* gate, void* stream);
+
+/* ------------------------------------------------------------------------- */
+/* RWKV-4 model                                                               */
+/* ------------------------------------------------------------------------- */
+enum kb_wkv_convention {
+    KB_WKV_STEP_REF = 0,   /* scripts/rwkv4_step_ref.py:76-94 (default)       */
+    KB_WKV_PRODUCTION = 1  /* krunch_ac/cuda/wkv_kernel.cu:57-72               */
+};
+
+typedef struct kb_layer_desc {
+    const float* ln1_w; const float* ln1_b;       /* [C] */
+    const float* ln2_w; const float* ln2_b;       /* [C] */
+    const float* att_mix_k; const float* att_mix_v; const float* att_mix_r; /* [C] */
+    const float* att_decay;  /* [C] exp(time_decay): ww2 = pp - decay           */
+    const float* att_first;  /* [C] time_first                                  */
+    const void* att_kw; const void* att_vw; const void* att_rw; const void* att_ow; /* [C,C] K-major */
+    const float* ffn_mix_k; const float* ffn_mix_r; /* [C] */
+    const void* ffn_kw;  /* [F,C] */
+    const void* ffn_vw;  /* [C,F] */
+    const void* ffn_rw;  /* [C,C] */
+} kb_layer_desc;
+
+typedef struct kb_model_desc {
+    int n_layer, n_embd, n_ffn, n_vocab;
+    int vocab_pad;       /* head rows, multiple of 128, >= n_vocab           */
+    int wdtype;          /* kb_dtype of the matrices                          */
+    int wkv_convention;  /* kb_wkv_convention                                 */
+    const uint16_t* emb; /* fp16 [n_vocab, C]                                 */
+    const float* ln_out_w; const float* ln_out_b;
+    const void* head;    /* [vocab_pad, C] K-major, rows >= n_vocab zero       */
+    const kb_layer_desc* layers; /* n_layer entries (copied at create)        */
+} kb_model_desc;
+
+typedef struct kb_model kb_model;
+
+/* Validates the description and copies it into an opaque host-side handle
+ * (no device allocation).  Replaces cpp_path.init_weights
+ * (krunch/cpp_path.py:26-91) on the native side. */
+int kb_model_create(const kb_model_desc* desc, kb_model** out);
+void kb_model_destroy(kb_model* model);
+
+/* exp(time_decay) with the library's own fixed-order exp, so encoder and
+ * decoder hosts derive identical decay constants. */
+int kb_prepare_decay(const float* time_decay, float* decay_out, int n, void* stream);
+
+/* Recurrent state: fp32 [n_layer][5][B][C]; slot 0 att_xx, 1 aa, 2 bb, 3 pp,
+ * 4 ffn_xx (the 5-per-layer contract of cpp_path.fresh_state,
+ * krunch/cpp_path.py:94-106, init_state_batched batched_rwkv4.py:60-82). */
+int kb_state_init(const kb_model* model, float* state, int B, void* stream);
+
+size_t kb_forward_workspace_bytes(const kb_model* model, int B, int T);
+
+/* Packed forward of a window: tokens int32 [B, T] (inputs), state as above
+ * (read and updated), logits fp16 [B*T, vocab_pad] (row b*T+t).  T = 1 is the
+ * stepped decompress forward; the same kernels run for every T, which makes
+ * packed and stepped logits bit-identical.  Replaces forward_packed_window /
+ * forward_stepped_batched (krunch/cpp_path.py:131-163,428-460) and
+ * rwkv4_layer_step_cpp (layer_cpp.cpp:456-637). */
+int kb_forward_window(const kb_model* model, const int32_t* tokens, int B, int T,
+                      float* state, void* workspace, size_t workspace_bytes,
+                      uint16_t* logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KRUNCH_B200_H */

@@ -1,0 +1,259 @@
+// RWKV-4 window forward: the orchestration that replaces cpp_path.py's
+// forward_packed_window / forward_stepped_batched and layer_cpp.cpp's
+// rwkv4_layer_step_cpp.  One code path for every window length T: T = 1 is
+// the stepped decoder, T > 1 the packed encoder.
+#include <new>
+#include <vector>
+
+#include "profile.cuh"
+#include "rwkv_ops.cuh"
+
+namespace kb {
+
+static thread_local int g_last_cuda_error = 0;
+void set_cuda_error(cudaError_t e) { g_last_cuda_error = (int)e; }
+
+// ---- phase profiler (single host thread) ----------------------------------
+namespace {
+struct ProfRec {
+    int phase;
+    cudaEvent_t a, b;
+    double work;
+};
+struct Prof {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<ProfRec> recs;
+};
+Prof g_prof;
+}  // namespace
+
+bool prof_on() { return g_prof.on; }
+cudaEvent_t prof_event() {
+    if (g_prof.used == g_prof.pool.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+        g_prof.pool.push_back(e);
+    }
+    return g_prof.pool[g_prof.used++];
+}
+void prof_push(int phase, cudaEvent_t a, cudaEvent_t b, double work) {
+    g_prof.recs.push_back({phase, a, b, work});
+}
+
+}  // namespace kb
+
+struct kb_model {
+    kb_model_desc d;
+    std::vector<kb_layer_desc> layers;
+};
+
+using namespace kb;
+
+extern "C" int kb_profile_begin(void) {
+    g_prof.on = true;
+    g_prof.used = 0;
+    g_prof.recs.clear();
+    return KB_OK;
+}
+
+extern "C" int kb_profile_end(double* ms, int64_t* launches, double* work, int n_phases) {
+    g_prof.on = false;
+    if (n_phases < 0 || ((!ms || !launches || !work) && n_phases > 0)) return KB_ERR_ARG;
+    for (int i = 0; i < n_phases; ++i) {
+        ms[i] = 0.0;
+        launches[i] = 0;
+        work[i] = 0.0;
+    }
+    for (const ProfRec& r : g_prof.recs) {
+        if (cudaEventSynchronize(r.b) != cudaSuccess) return launch_status();
+        float t = 0.f;
+        if (cudaEventElapsedTime(&t, r.a, r.b) != cudaSuccess) return launch_status();
+        if (r.phase < n_phases) {
+            ms[r.phase] += t;
+            launches[r.phase] += 1;
+            work[r.phase] += r.work;
+        }
+    }
+    g_prof.recs.clear();
+    g_prof.used = 0;
+    return KB_OK;
+}
+
+extern "C" const char* kb_version(void) { return "krunch_b200 0.1.0 (sm_100a)"; }
+
+extern "C" int kb_last_cuda_error(void) { return g_last_cuda_error; }
+
+extern "C" const char* kb_status_string(int s) {
+    switch (s) {
+        case KB_OK: return "ok";
+        case KB_ERR_ARG: return "invalid argument";
+        case KB_ERR_SHAPE: return "unsupported shape";
+        case KB_ERR_ALIGN: return "misaligned pointer or stride";
+        case KB_ERR_CUDA: return "CUDA error";
+        case KB_ERR_TIMEOUT: return "device wait timed out";
+        case KB_ERR_UNSUPPORTED: return "unsupported on this build";
+        case KB_ERR_WORKSPACE: return "workspace too small";
+        case KB_ERR_NOMEM: return "host allocation failed";
+        default: return "unknown status";
+    }
+}
+
+static bool al16(const void* p) { return p && aligned16(p); }
+
+extern "C" int kb_model_create(const kb_model_desc* d, kb_model** out) {
+    if (!d || !out) return KB_ERR_ARG;
+    *out = nullptr;
+    const int C = d->n_embd, F = d->n_ffn;
+    if (d->n_layer < 1 || C < 128 || F < 128 || d->n_vocab < 2) return KB_ERR_ARG;
+    if (C % 128 || F % 128 || C > 4096) return KB_ERR_SHAPE;
+    if (d->vocab_pad < d->n_vocab || d->vocab_pad % 128 || d->n_vocab > 65536) return KB_ERR_SHAPE;
+    if (d->wdtype != KB_F16) return KB_ERR_UNSUPPORTED;
+    if (d->wkv_convention != KB_WKV_STEP_REF && d->wkv_convention != KB_WKV_PRODUCTION)
+        return KB_ERR_ARG;
+    if (!al16(d->emb) || !d->ln_out_w || !d->ln_out_b || !al16(d->head) || !d->layers)
+        return KB_ERR_ARG;
+    for (int l = 0; l < d->n_layer; ++l) {
+        const kb_layer_desc& L = d->layers[l];
+        if (!L.ln1_w || !L.ln1_b || !L.ln2_w || !L.ln2_b || !L.att_mix_k || !L.att_mix_v ||
+            !L.att_mix_r || !L.att_decay || !L.att_first || !L.ffn_mix_k || !L.ffn_mix_r)
+            return KB_ERR_ARG;
+        if (!al16(L.att_kw) || !al16(L.att_vw) || !al16(L.att_rw) || !al16(L.att_ow) ||
+            !al16(L.ffn_kw) || !al16(L.ffn_vw) || !al16(L.ffn_rw))
+            return KB_ERR_ALIGN;
+    }
+    kb_model* m = new (std::nothrow) kb_model;
+    if (!m) return KB_ERR_NOMEM;
+    m->d = *d;
+    m->layers.assign(d->layers, d->layers + d->n_layer);
+    m->d.layers = m->layers.data();
+    *out = m;
+    return KB_OK;
+}
+
+extern "C" void kb_model_destroy(kb_model* m) { delete m; }
+
+extern "C" int kb_state_init(const kb_model* m, float* state, int B, void* stream) {
+    if (!m || !state || B < 0) return KB_ERR_ARG;
+    return launch_state_init(state, m->d.n_layer, B, m->d.n_embd, as_stream(stream));
+}
+
+namespace {
+
+struct Workspace {
+    uint16_t *x, *kx, *vx, *rx, *r, *ry, *kk;
+    float *k, *v, *xx_att, *xx_ffn;
+};
+
+inline size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+size_t layout(const kb_model_desc& d, int B, int T, char* base, Workspace* w) {
+    const size_t R = (size_t)B * T, C = d.n_embd, F = d.n_ffn;
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> char* {
+        char* p = base ? base + off : nullptr;
+        off += al256(bytes);
+        return p;
+    };
+    Workspace t;
+    t.x = (uint16_t*)take(R * C * 2);
+    t.kx = (uint16_t*)take(R * C * 2);
+    t.vx = (uint16_t*)take(R * C * 2);
+    t.rx = (uint16_t*)take(R * C * 2);
+    t.r = (uint16_t*)take(R * C * 2);
+    t.ry = (uint16_t*)take(R * C * 2);
+    t.kk = (uint16_t*)take(R * F * 2);
+    t.k = (float*)take(R * C * 4);
+    t.v = (float*)take(R * C * 4);
+    t.xx_att = (float*)take((size_t)B * C * 4);
+    t.xx_ffn = (float*)take((size_t)B * C * 4);
+    if (w) *w = t;
+    return off;
+}
+
+#define KB_TRY(expr)                 \
+    do {                             \
+        const int _s = (expr);       \
+        if (_s != KB_OK) return _s;  \
+    } while (0)
+
+}  // namespace
+
+extern "C" size_t kb_forward_workspace_bytes(const kb_model* m, int B, int T) {
+    if (!m || B <= 0 || T <= 0) return 0;
+    return layout(m->d, B, T, nullptr, nullptr);
+}
+
+extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B, int T,
+                                 float* state, void* ws, size_t ws_bytes, uint16_t* logits,
+                                 void* stream) {
+    if (!m || !tokens || !state || !ws || !logits || B <= 0 || T <= 0) return KB_ERR_ARG;
+    const kb_model_desc& d = m->d;
+    if (ws_bytes < layout(d, B, T, nullptr, nullptr)) return KB_ERR_WORKSPACE;
+    if (!aligned16(ws) || !aligned16(logits)) return KB_ERR_ALIGN;
+    cudaStream_t st = as_stream(stream);
+    Workspace w;
+    layout(d, B, T, reinterpret_cast<char*>(ws), &w);
+    const int C = d.n_embd, F = d.n_ffn;
+    const int R = B * T;
+    const size_t BC = (size_t)B * C;
+
+    const double bpe = 2.0;  // fp16 bytes per element
+    auto gemm = [&](const uint16_t* A, const void* W, int M, int Nn, int K, int epi, void* out,
+                    const uint16_t* resid, const uint16_t* gate, int phase) -> int {
+        ProfScope ps(phase, st, 2.0 * M * (double)Nn * K);
+        return launch_gemm_f16(A, K, (const uint16_t*)W, K, M, Nn, K, epi, out, Nn, resid, gate, st);
+    };
+    {
+        ProfScope ps(PH_EMBED, st, (double)R * C * 2 * bpe);
+        KB_TRY(launch_embed(tokens, R, d.n_vocab, C, d.emb, w.x, st));
+    }
+    for (int l = 0; l < d.n_layer; ++l) {
+        const kb_layer_desc& L = d.layers[l];
+        float* s = state + (size_t)l * 5 * BC;
+        float *s_att = s, *s_aa = s + BC, *s_bb = s + 2 * BC, *s_pp = s + 3 * BC,
+              *s_ffn = s + 4 * BC;
+
+        // ---- time mix -------------------------------------------------------
+        MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx}};
+        {
+            ProfScope ps(PH_LN_MIX, st, (double)R * C * 4 * bpe);
+            KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
+        }
+        KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        {
+            ProfScope ps(PH_WKV, st, (double)R * C * 12.0);
+            KB_TRY(launch_wkv(d.wkv_convention, B, T, C, w.k, w.v, w.r, L.att_decay, L.att_first,
+                              s_aa, s_bb, s_pp, w.ry, st));
+        }
+        KB_TRY(gemm(w.ry, L.att_ow, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+        if (cudaMemcpyAsync(s_att, w.xx_att, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return launch_status();
+
+        // ---- channel mix ----------------------------------------------------
+        MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr}};
+        {
+            ProfScope ps(PH_LN_MIX, st, (double)R * C * 3 * bpe);
+            KB_TRY(launch_ln_mix(2, w.x, B, T, C, L.ln2_w, L.ln2_b, mf, s_ffn, w.xx_ffn, nullptr, st));
+        }
+        KB_TRY(gemm(w.rx, L.ffn_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.kx, L.ffn_kw, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.kk, L.ffn_vw, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+        if (cudaMemcpyAsync(s_ffn, w.xx_ffn, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+            return launch_status();
+    }
+    MixArgs none{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}};
+    {
+        ProfScope ps(PH_LN_MIX, st, (double)R * C * 2 * bpe);
+        KB_TRY(launch_ln_mix(0, w.x, B, T, C, d.ln_out_w, d.ln_out_b, none, nullptr, nullptr, w.kx, st));
+    }
+    {
+        ProfScope ps(PH_HEAD, st, 2.0 * R * (double)d.n_vocab * C);
+        KB_TRY(launch_gemm_f16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C, KB_EPI_F16,
+                               logits, d.vocab_pad, nullptr, nullptr, st));
+    }
+    return KB_OK;
+}

@@ -1,0 +1,30 @@
+// Launchers of the RWKV-4 row-local / recurrent kernels (rwkv_ops.cu) and
+// the GEMM family (gemm.cu), used by the forward orchestration (forward.cu).
+#pragma once
+#include <algorithm>
+
+#include "kb_common.cuh"
+
+namespace kb {
+
+struct MixArgs {
+    const float* mix[3];  // time-mix vectors [C]
+    uint16_t* out[3];     // fp16 [rows, C] outputs
+};
+
+int launch_embed(const int32_t* tok, int64_t rows, int V, int C, const uint16_t* emb, uint16_t* x,
+                 cudaStream_t st);
+int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float* lw,
+                  const float* lb, const MixArgs& ma, const float* state_in, float* state_out,
+                  uint16_t* xx_out, cudaStream_t st);
+int launch_wkv(int conv, int B, int T, int C, const float* k, const float* v, const uint16_t* r,
+               const float* decay, const float* first, float* aa, float* bb, float* pp,
+               uint16_t* ry, cudaStream_t st);
+int launch_state_init(float* st, int L, int B, int C, cudaStream_t s);
+
+// out[M,N] = epi(A[M,K] @ W[N,K]^T); see kb_gemm in the public header.
+int launch_gemm_f16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
+                    int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
+                    const uint16_t* gate, cudaStream_t st);
+
+}  // namespace kb

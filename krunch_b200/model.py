@@ -1,0 +1,160 @@
+"""RWKV-4 model resident on one B200: device weights + the native model handle.
+
+Replaces krunch/cpp_path.py:init_weights / fresh_state (cpp_path.py:26-106).
+Weights arrive in the reference's ``model.w`` layout (matrices [in, out],
+time_decay as the raw log-decay of rwkv4_step_ref.py:89) and are stored on
+the device K-major ([out, in], fp16) for the GEMMs.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _native as N
+
+
+@dataclass(frozen=True)
+class ModelSpec:
+    n_layer: int
+    n_embd: int
+    n_ffn: int
+    n_vocab: int
+    wdtype: str = "f16"
+    wkv: str = "step_ref"
+
+    @property
+    def vocab_pad(self) -> int:
+        return (self.n_vocab + 127) // 128 * 128
+
+
+def _n_layer(w: dict) -> int:
+    n = 0
+    while f"blocks.{n}.ln1.weight" in w:
+        n += 1
+    return n
+
+
+class RWKVModel:
+    """Device-resident RWKV-4 with a kb_model handle."""
+
+    def __init__(self, w: dict, device="cuda", wkv: str = "step_ref", wdtype: str = "f16"):
+        if wdtype != "f16":
+            raise NotImplementedError(f"weight dtype {wdtype!r} is not built yet")
+        if wkv not in ("step_ref", "production"):
+            raise ValueError(f"unknown WKV convention {wkv!r}")
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise RuntimeError("krunch_b200 runs on CUDA devices only")
+        L = _n_layer(w)
+        V, Cm = w["emb.weight"].shape
+        F = w["blocks.0.ffn.key.weight"].shape[1]
+        self.spec = ModelSpec(L, Cm, F, V, wdtype, wkv)
+        self._keep: list[torch.Tensor] = []
+        dev = self.device
+
+        def f32(a):
+            t = torch.as_tensor(np.ascontiguousarray(a, dtype=np.float32).reshape(-1)).to(dev)
+            self._keep.append(t)
+            return t
+
+        def kmajor(a):  # [in, out] -> fp16 [out, in]
+            t = torch.as_tensor(np.asarray(a, dtype=np.float32)).to(dev)
+            t = t.t().contiguous().to(torch.float16)
+            self._keep.append(t)
+            return t
+
+        stream = N.stream_ptr(dev)
+        self.emb = torch.as_tensor(np.asarray(w["emb.weight"], np.float32)).to(dev).half().contiguous()
+        self._keep.append(self.emb)
+        layers = (N.LayerDesc * L)()
+        for i in range(L):
+            b, att, ffn = f"blocks.{i}.", f"blocks.{i}.att.", f"blocks.{i}.ffn."
+            td = f32(w[att + "time_decay"])
+            decay = torch.empty_like(td)
+            self._keep.append(decay)
+            N.call("kb_prepare_decay", td.data_ptr(), decay.data_ptr(), td.numel(), stream)
+            d = layers[i]
+            d.ln1_w, d.ln1_b = f32(w[b + "ln1.weight"]).data_ptr(), f32(w[b + "ln1.bias"]).data_ptr()
+            d.ln2_w, d.ln2_b = f32(w[b + "ln2.weight"]).data_ptr(), f32(w[b + "ln2.bias"]).data_ptr()
+            d.att_mix_k = f32(w[att + "time_mix_k"]).data_ptr()
+            d.att_mix_v = f32(w[att + "time_mix_v"]).data_ptr()
+            d.att_mix_r = f32(w[att + "time_mix_r"]).data_ptr()
+            d.att_decay = decay.data_ptr()
+            d.att_first = f32(w[att + "time_first"]).data_ptr()
+            d.att_kw = kmajor(w[att + "key.weight"]).data_ptr()
+            d.att_vw = kmajor(w[att + "value.weight"]).data_ptr()
+            d.att_rw = kmajor(w[att + "receptance.weight"]).data_ptr()
+            d.att_ow = kmajor(w[att + "output.weight"]).data_ptr()
+            d.ffn_mix_k = f32(w[ffn + "time_mix_k"]).data_ptr()
+            d.ffn_mix_r = f32(w[ffn + "time_mix_r"]).data_ptr()
+            d.ffn_kw = kmajor(w[ffn + "key.weight"]).data_ptr()
+            d.ffn_vw = kmajor(w[ffn + "value.weight"]).data_ptr()
+            d.ffn_rw = kmajor(w[ffn + "receptance.weight"]).data_ptr()
+        Vp = self.spec.vocab_pad
+        head = torch.zeros((Vp, Cm), dtype=torch.float16, device=dev)
+        head[:V] = torch.as_tensor(np.asarray(w["head.weight"], np.float32)).to(dev).t().half()
+        self.head = head
+        self._keep.append(head)
+        self._layers = layers
+        desc = N.ModelDesc()
+        desc.n_layer, desc.n_embd, desc.n_ffn, desc.n_vocab = L, Cm, F, V
+        desc.vocab_pad = Vp
+        desc.wdtype = N.KB_F16
+        desc.wkv_convention = N.KB_WKV_STEP_REF if wkv == "step_ref" else N.KB_WKV_PRODUCTION
+        desc.emb = self.emb.data_ptr()
+        desc.ln_out_w = f32(w["ln_out.weight"]).data_ptr()
+        desc.ln_out_b = f32(w["ln_out.bias"]).data_ptr()
+        desc.head = head.data_ptr()
+        desc.layers = layers
+        handle = C.c_void_p()
+        N.call("kb_model_create", C.byref(desc), C.byref(handle))
+        self.handle = handle
+        torch.cuda.synchronize(dev)
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                N.load().kb_model_destroy(h)
+            except Exception:
+                pass
+            self.handle = None
+
+    # ------------------------------------------------------------------ state
+    def state_numel(self, B: int) -> int:
+        s = self.spec
+        return s.n_layer * 5 * B * s.n_embd
+
+    def new_state(self, B: int) -> torch.Tensor:
+        """fp32 [n_layer, 5, B, C]: att_xx, aa, bb, pp (-1e30), ffn_xx."""
+        s = self.spec
+        st = torch.empty((s.n_layer, 5, B, s.n_embd), dtype=torch.float32, device=self.device)
+        N.call("kb_state_init", self.handle, st.data_ptr(), B, N.stream_ptr(self.device))
+        return st
+
+    # ---------------------------------------------------------------- forward
+    def workspace_bytes(self, B: int, T: int) -> int:
+        return int(N.load().kb_forward_workspace_bytes(self.handle, B, T))
+
+    def new_workspace(self, B: int, T: int) -> torch.Tensor:
+        return torch.empty(self.workspace_bytes(B, T), dtype=torch.uint8, device=self.device)
+
+    def new_logits(self, B: int, T: int) -> torch.Tensor:
+        return torch.empty((B * T, self.spec.vocab_pad), dtype=torch.float16, device=self.device)
+
+    def forward_window(self, tokens: torch.Tensor, state: torch.Tensor, workspace: torch.Tensor,
+                       logits: torch.Tensor) -> torch.Tensor:
+        """tokens int32 [B, T] (contiguous, on device) -> logits fp16 [B*T, vocab_pad].
+
+        ``state`` is read and advanced in place."""
+        B, T = tokens.shape
+        assert tokens.dtype == torch.int32 and tokens.is_contiguous()
+        assert state.is_contiguous() and state.numel() == self.state_numel(B)
+        assert logits.shape[0] >= B * T and logits.shape[1] == self.spec.vocab_pad
+        N.call("kb_forward_window", self.handle, tokens.data_ptr(), B, T, state.data_ptr(),
+               workspace.data_ptr(), workspace.numel(), logits.data_ptr(),
+               N.stream_ptr(self.device))
+        return logits

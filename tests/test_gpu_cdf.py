@@ -1,0 +1,122 @@
+"""Fused logits -> integer CDF kernel: bit-exact against the C oracle (same
+fixed reduction order), batch-invariant (scripts/test_det_softmax_cdf.py:18-41
+of the reference), and the fused decode step round-trips."""
+import numpy as np
+import pytest
+
+from helpers import random_logits
+from oracle import coder
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    return t
+
+
+def _cdf_gpu(torch, logits_np, bits, mode=1, stride=None, symbols=None):
+    from krunch_b200 import _native as N
+    rows, V = logits_np.shape
+    stride = stride or V
+    buf = np.zeros((rows, stride), np.float16)
+    buf[:, :V] = logits_np
+    x = torch.from_numpy(buf).cuda()
+    if mode == N.KB_CDF_LOHI:
+        out = torch.empty((rows, 2), dtype=torch.int32, device="cuda")
+        sym = torch.from_numpy(symbols.astype(np.int32)).cuda()
+        N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, sym.data_ptr(),
+               out.data_ptr(), N.stream_ptr())
+        return out.cpu().numpy().view(np.uint32)
+    out = torch.empty((rows, V + 1), dtype=torch.int32, device="cuda")
+    N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, None, out.data_ptr(),
+           N.stream_ptr())
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("bits", [16, 24])
+@pytest.mark.parametrize("V,stride", [(4, 4), (32, 40), (300, 384), (1000, 1000), (50277, 50304),
+                                      (50277, 50277), (511, 513), (513, 513)])
+def test_cdf_bit_exact_vs_oracle(torch, V, stride, bits):
+    x = random_logits(6, V, seed=V + bits)
+    x[0] = 0  # all-equal row: argmax tie -> index 0
+    x[1, V // 2] = 30  # peaked row
+    got = _cdf_gpu(torch, x, bits, stride=stride)
+    want = coder.cdf_from_logits(x, bits)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("bits", [16, 24])
+def test_counts_and_lohi_modes(torch, bits):
+    from krunch_b200 import _native as N
+    V = 5000
+    x = random_logits(9, V, seed=3)
+    cdf = coder.cdf_from_logits(x, bits)
+    cnt = _cdf_gpu(torch, x, bits, mode=N.KB_CDF_COUNTS)
+    assert cnt[:, 0].tolist() == [0] * 9
+    assert np.array_equal(np.cumsum(cnt, axis=1), cdf)
+    sym = np.random.default_rng(0).integers(0, V, 9)
+    lh = _cdf_gpu(torch, x, bits, mode=N.KB_CDF_LOHI, symbols=sym)
+    assert np.array_equal(lh, coder.lohi_from_logits(x, sym, bits))
+
+
+def test_batch_invariance(torch):
+    """Rows computed in a batch of R equal rows computed one at a time."""
+    x = random_logits(33, 50277, seed=11)
+    full = _cdf_gpu(torch, x, 16)
+    for r in (0, 7, 32):
+        assert np.array_equal(_cdf_gpu(torch, x[r:r + 1], 16), full[r:r + 1])
+
+
+@pytest.mark.parametrize("bits", [16, 24])
+def test_from_probs_bit_exact(torch, bits):
+    from krunch_b200.krunch_ac import probs_to_cdf
+    from helpers import rand_probs
+    p = rand_probs(64, 256, 1)
+    got = probs_to_cdf(p, bits)
+    assert got.dtype == np.uint32
+    assert np.array_equal(got.astype(np.int64), coder.cdf_from_probs(p, bits).astype(np.int64))
+
+
+@pytest.mark.parametrize("bits", [16, 24])
+def test_fused_decode_step_roundtrip(torch, bits):
+    """Encode with the oracle from logits; decode on the GPU from the same
+    logits with the fused CDF+search+coder kernel, ragged stream lengths."""
+    from krunch_b200 import _native as N
+    B, T, V, Vp = 4, 40, 3000, 3072
+    lens = [40, 1, 25, 0]
+    rng = np.random.default_rng(9)
+    logits = (rng.standard_normal((T, B, V)) * 3).astype(np.float16)
+    sym = rng.integers(0, V, (B, T)).astype(np.int32)
+    streams = []
+    for b in range(B):
+        lh = coder.lohi_from_logits(logits[:lens[b], b], sym[b, :lens[b]], bits)
+        streams.append(coder.encode_lohi(lh, bits))
+    offs, pos = [], 0
+    for s in streams:
+        offs.append(pos)
+        pos += len(s) + 64
+    cat = np.zeros(pos, np.uint8)
+    for o, s in zip(offs, streams):
+        cat[o:o + len(s)] = np.frombuffer(s, np.uint8)
+    inb = torch.from_numpy(cat).cuda()
+    offs_t = torch.tensor(offs, dtype=torch.int64, device="cuda")
+    st = torch.empty(B * 4, dtype=torch.int32, device="cuda")
+    cnt = torch.tensor([[0, n] for n in lens], dtype=torch.int32, device="cuda")
+    cur = torch.zeros(B, dtype=torch.int32, device="cuda")
+    hist = torch.full((B, T), -1, dtype=torch.int32, device="cuda")
+    sp = N.stream_ptr()
+    N.call("kb_coder_decode_init", inb.data_ptr(), inb.numel(), offs_t.data_ptr(), st.data_ptr(), B, sp)
+    lg = np.zeros((B, Vp), np.float16)
+    for t in range(T):
+        lg[:, :V] = logits[t]
+        x = torch.from_numpy(lg).cuda()
+        N.call("kb_decode_logits_step", x.data_ptr(), Vp, B, V, bits, inb.data_ptr(), inb.numel(),
+               offs_t.data_ptr(), st.data_ptr(), cnt.data_ptr(), cur.data_ptr(), hist.data_ptr(),
+               T, sp)
+    h = hist.cpu().numpy()
+    for b in range(B):
+        assert h[b, :lens[b]].tolist() == sym[b, :lens[b]].tolist()
+        assert (h[b, lens[b]:] == -1).all()
+    assert cnt[:, 0].cpu().tolist() == lens

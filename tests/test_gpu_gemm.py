@@ -1,0 +1,68 @@
+"""GEMM + fused epilogues against a plain PyTorch fp32 reference, and the
+M-invariance contract (reference scripts/test_det_matmul_tc_mw.py:20-39:
+a row's bits do not depend on M)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    return t
+
+
+def _gemm(torch, A, W, epi, resid=None, gate=None, out_dtype=None):
+    from krunch_b200 import _native as N
+    M, K = A.shape
+    Nn = W.shape[0]
+    dt = torch.float32 if epi == N.KB_EPI_F32 else torch.float16
+    out = resid.clone() if resid is not None else torch.empty((M, Nn), dtype=dt, device="cuda")
+    N.call("kb_gemm", N.KB_F16, A.data_ptr(), K, W.data_ptr(), K, M, Nn, K, epi, out.data_ptr(),
+           Nn, None if resid is None else out.data_ptr(), None if gate is None else gate.data_ptr(),
+           N.stream_ptr())
+    return out
+
+
+def _ref(torch, A, W, epi, resid=None, gate=None):
+    from krunch_b200 import _native as N
+    acc = A.float() @ W.float().t()
+    if epi == N.KB_EPI_SIGMOID:
+        return torch.sigmoid(acc)
+    if epi == N.KB_EPI_RELU_SQ:
+        return torch.relu(acc) ** 2
+    if epi == N.KB_EPI_RESID:
+        return resid.float() + acc
+    if epi == N.KB_EPI_GATE_RESID:
+        return resid.float() + gate.float() * acc
+    return acc
+
+
+@pytest.mark.parametrize("epi", range(6))
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (77, 256, 192), (300, 768, 768), (1000, 384, 3072)])
+def test_gemm_epilogues_vs_torch_fp32(torch, epi, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K + epi)
+    A = (torch.randn((M, K), device="cuda", generator=g) * 0.5).half()
+    W = (torch.randn((N, K), device="cuda", generator=g) * 0.05).half()
+    resid = torch.randn((M, N), device="cuda", generator=g).half()
+    gate = torch.rand((M, N), device="cuda", generator=g).half()
+    out = _gemm(torch, A, W, epi, resid if epi >= 4 else None, gate if epi == 5 else None)
+    ref = _ref(torch, A, W, epi, resid, gate)
+    tol = 1e-4 if epi == 0 else 2e-2
+    err = (out.float() - ref).abs().max().item()
+    assert err <= tol * max(1.0, ref.abs().max().item()), err
+
+
+def test_m_invariance(torch):
+    from krunch_b200 import _native as N
+    g = torch.Generator(device="cuda").manual_seed(1)
+    K, Nn = 768, 768
+    A = (torch.randn((1000, K), device="cuda", generator=g)).half()
+    W = (torch.randn((Nn, K), device="cuda", generator=g) * 0.03).half()
+    full = _gemm(torch, A, W, N.KB_EPI_F32)
+    for M in (1, 16, 64, 128, 129, 256, 999):
+        part = _gemm(torch, A[:M].contiguous(), W, N.KB_EPI_F32)
+        assert torch.equal(part, full[:M]), M
+    rows = A[[5, 900, 3]].contiguous()
+    assert torch.equal(_gemm(torch, rows, W, N.KB_EPI_F32), full[[5, 900, 3]])

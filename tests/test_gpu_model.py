@@ -1,0 +1,97 @@
+"""RWKV-4 forward on the GPU.
+
+* logits vs the reference's rwkv4_step_ref / forward_batched (golden files)
+  within BASELINE's 2e-2 max-abs (fp16 kernels vs fp32 reference);
+* packed vs stepped, window composition and batch invariance are
+  BIT-identical (reference scripts/test_full_model_packed_vs_stepped.py:77-110,
+  test_multi_window_roundtrip.py, test_batched_stepped.py:49-109)."""
+import numpy as np
+import pytest
+
+from krunch_b200.synth import random_weights
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    return t
+
+
+@pytest.fixture(scope="module")
+def tiny(torch):
+    from krunch_b200.model import RWKVModel
+    return RWKVModel(random_weights(2, 128, 512, 300, seed=0))
+
+
+def _run(torch, m, tokens, state=None):
+    tok = torch.from_numpy(np.ascontiguousarray(tokens, dtype=np.int32)).cuda()
+    B, T = tok.shape
+    st = m.new_state(B) if state is None else state
+    lg = m.new_logits(B, T)
+    m.forward_window(tok, st, m.new_workspace(B, T), lg)
+    return lg[:, :m.spec.n_vocab].float().view(B, T, -1).cpu().numpy(), st
+
+
+def test_tiny_logits_vs_reference(torch, tiny, golden_dir):
+    g = np.load(golden_dir / "model_tiny.npz")
+    st = tiny.new_state(1)
+    outs = []
+    for t in g["stepped_tokens"]:
+        lg, st = _run(torch, tiny, [[t]], st)
+        outs.append(lg[0, 0])
+    assert np.abs(np.stack(outs) - g["stepped"]).max() <= LOGIT_TOL
+    lg, _ = _run(torch, tiny, g["packed_tokens"])
+    assert np.abs(lg - g["packed"]).max() <= LOGIT_TOL
+
+
+def test_169m_logits_vs_reference(torch, golden_dir):
+    from krunch_b200.model import RWKVModel
+    g = np.load(golden_dir / "model_169m.npz")
+    m = RWKVModel(random_weights(12, 768, 3072, 50277, seed=int(g["seed"])))
+    st = m.new_state(1)
+    outs = []
+    for t in g["stepped_tokens"]:
+        lg, st = _run(torch, m, [[t]], st)
+        outs.append(lg[0, 0])
+    o = np.stack(outs)
+    assert np.abs(o[:, :256] - g["stepped_head256"]).max() <= LOGIT_TOL
+    assert np.abs(o.max(1) - g["stepped_max"]).max() <= LOGIT_TOL
+    lg, _ = _run(torch, m, g["packed_tokens"])
+    f = lg.reshape(-1, lg.shape[-1])
+    assert np.abs(f[:, :256] - g["packed_head256"]).max() <= LOGIT_TOL
+
+
+@pytest.mark.parametrize("wkv", ["step_ref", "production"])
+def test_packed_equals_stepped_bitwise(torch, wkv):
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=5), wkv=wkv)
+    tok = np.random.default_rng(1).integers(0, 300, (3, 20))
+    packed, st_p = _run(torch, m, tok)
+    st = m.new_state(3)
+    steps = []
+    for t in range(20):
+        lg, st = _run(torch, m, tok[:, t:t + 1], st)
+        steps.append(lg[:, 0])
+    assert np.array_equal(np.stack(steps, 1), packed)
+    assert torch.equal(st, st_p)
+    # window composition 7 + 13
+    a, st2 = _run(torch, m, tok[:, :7])
+    b, st2 = _run(torch, m, tok[:, 7:], st2)
+    assert np.array_equal(np.concatenate([a, b], 1), packed)
+    # batch invariance: stream 1 alone
+    one, _ = _run(torch, m, tok[1:2])
+    assert np.array_equal(one[0], packed[1])
+
+
+def test_production_convention_vs_oracle(torch):
+    from krunch_b200.model import RWKVModel
+    from oracle import rwkv
+    w = random_weights(2, 128, 512, 300, seed=6)
+    m = RWKVModel(w, wkv="production")
+    tok = np.random.default_rng(2).integers(0, 300, (2, 9))
+    lg, _ = _run(torch, m, tok)
+    ref, _ = rwkv.forward(w, tok, wkv="production")
+    assert np.abs(lg - ref).max() <= LOGIT_TOL
