@@ -35,7 +35,8 @@ enum kb_status {
     KB_ERR_TIMEOUT = -5,     /* bounded device wait expired                   */
     KB_ERR_UNSUPPORTED = -6, /* feature not built for this device             */
     KB_ERR_WORKSPACE = -7,   /* workspace smaller than the query returned     */
-    KB_ERR_NOMEM = -8        /* host allocation failed (model handle)         */
+    KB_ERR_NOMEM = -8,       /* host allocation failed (model handle)         */
+    KB_ERR_TOO_LARGE = -9    /* request exceeds the fixed no-alloc scratch    */
 };
 
 const char* kb_version(void);
@@ -238,6 +239,29 @@ size_t kb_forward_workspace_bytes(const kb_model* model, int B, int T);
 int kb_forward_window(const kb_model* model, const int32_t* tokens, int B, int T,
                       float* state, void* workspace, size_t workspace_bytes,
                       uint16_t* logits, void* stream);
+
+/* Allocation-free variant of kb_forward_window.  No counterpart in the
+ * reference: it exists for hosts that cannot allocate device memory when they
+ * run a forward, e.g. a decode loop being recorded into a CUDA graph (device
+ * allocation is not allowed during stream capture), a foreign-language host
+ * (Go/JNI/Rust over this ABI) whose process runs under a fixed device-memory
+ * budget handed out at start-up, or a caller without a CUDA allocator of its
+ * own.  The caller still passes tokens, state and logits; the activation
+ * workspace lives in a file-scope __device__ array of
+ * KB_NOALLOC_SCRATCH_BYTES that every GPU loading this library keeps until
+ * process exit.
+ *   - The first call on a device resolves that array's device address (with
+ *     the device current), so make it before any stream capture begins.
+ *   - Windows whose workspace (kb_forward_workspace_bytes) exceeds the array
+ *     return KB_ERR_TOO_LARGE; 8 MiB covers B*T <= 384 rows of RWKV-4-169M.
+ *   - All calls share the one array and it keeps the previous call's
+ *     contents; nothing in it needs to start at zero.  Calls that can overlap
+ *     on the GPU (other streams, other host threads) race on it: serialise
+ *     them on one stream.
+ * Makes no cudaMalloc / cudaFree or allocating library call. */
+#define KB_NOALLOC_SCRATCH_BYTES ((size_t)8 << 20)
+int kb_forward_window_noalloc(const kb_model* model, const int32_t* tokens, int B, int T,
+                              float* state, uint16_t* logits, void* stream);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,8 @@ from pathlib import Path
 _LIB_PATH = Path(__file__).resolve().parent / "libkrunch_b200.so"
 
 KB_OK = 0
+KB_ERR_TOO_LARGE = -9
+KB_NOALLOC_SCRATCH_BYTES = 8 << 20
 KB_CDF_COUNTS, KB_CDF_CDF, KB_CDF_LOHI = 0, 1, 2
 KB_EPI_F32, KB_EPI_F16, KB_EPI_SIGMOID, KB_EPI_RELU_SQ, KB_EPI_RESID, KB_EPI_GATE_RESID = range(6)
 KB_F16, KB_BF16, KB_I8 = 0, 1, 2
@@ -63,6 +65,7 @@ SIGNATURES = {
     "kb_state_init": (i32, [vp, vp, i32, vp]),
     "kb_forward_workspace_bytes": (sz, [vp, i32, i32]),
     "kb_forward_window": (i32, [vp, vp, i32, i32, vp, vp, sz, vp, vp]),
+    "kb_forward_window_noalloc": (i32, [vp, vp, i32, i32, vp, vp, vp]),
 }
 
 _lib = None

@@ -2,6 +2,7 @@
 // forward_packed_window / forward_stepped_batched and layer_cpp.cpp's
 // rwkv4_layer_step_cpp.  One code path for every window length T: T = 1 is
 // the stepped decoder, T > 1 the packed encoder.
+#include <mutex>
 #include <new>
 #include <vector>
 
@@ -96,6 +97,7 @@ extern "C" const char* kb_status_string(int s) {
         case KB_ERR_UNSUPPORTED: return "unsupported on this build";
         case KB_ERR_WORKSPACE: return "workspace too small";
         case KB_ERR_NOMEM: return "host allocation failed";
+        case KB_ERR_TOO_LARGE: return "request exceeds the fixed no-alloc scratch";
         default: return "unknown status";
     }
 }
@@ -256,4 +258,50 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
                                logits, d.vocab_pad, nullptr, nullptr, st));
     }
     return KB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// kb_forward_window_noalloc: the same forward with its workspace in a fixed
+// device array, for callers that cannot allocate device memory.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device, resolved once
+// per device (host code must not use the symbol itself as a pointer).
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return KB_ERR_CUDA;
+    }
+    if (dev < 0 || dev >= kMaxDevices) return KB_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            set_cuda_error(e);
+            return KB_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return KB_OK;
+}
+}  // namespace
+
+extern "C" int kb_forward_window_noalloc(const kb_model* m, const int32_t* tokens, int B, int T,
+                                         float* state, uint16_t* logits, void* stream) {
+    if (!m || !tokens || !state || !logits || B <= 0 || T <= 0) return KB_ERR_ARG;
+    if (layout(m->d, B, T, nullptr, nullptr) > KB_NOALLOC_SCRATCH_BYTES) return KB_ERR_TOO_LARGE;
+    void* ws = nullptr;
+    const int rc = noalloc_scratch(&ws);
+    if (rc != KB_OK) return rc;
+    return kb_forward_window(m, tokens, B, T, state, ws, KB_NOALLOC_SCRATCH_BYTES, logits, stream);
 }
