@@ -174,10 +174,16 @@ enum kb_epilogue {
 enum kb_dtype { KB_F16 = 0, KB_BF16 = 1, KB_I8 = 2 };
 
 /* A, W: fp16 (dtype KB_F16).  resid/gate fp16 [M, ldo] (may alias out).
- * Requires N % 128 == 0, K % 64 == 0, 16-byte aligned rows. */
+ * Requires N % 32 == 0, K % 64 == 0, 16-byte aligned rows and out. */
 int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
             int M, int N, int K, int epilogue, void* out, int64_t ldo,
             const uint16_t* resid, const uint16_t* gate, void* stream);
+
+/* Device-side failure report of the tcgen05 kernels: every mbarrier wait in
+ * them is bounded, and a wait that expires records an error and makes the
+ * kernel unwind (no hang).  Returns KB_OK or KB_ERR_TIMEOUT (KB_ERR_CUDA if the
+ * flag cannot be read); reset != 0 clears the flag.  Synchronises the device. */
+int kb_device_error_status(int reset);
 
 /* ------------------------------------------------------------------------- */
 /* RWKV-4 model                                                               */

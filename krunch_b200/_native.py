@@ -58,6 +58,7 @@ SIGNATURES = {
     "kb_cdf_rows": (i32, [vp, i64, i32, i32, i32, i32, vp, vp, vp]),
     "kb_cdf_from_probs": (i32, [vp, i32, i32, i32, vp, vp]),
     "kb_decode_logits_step": (i32, [vp, i64, i32, i32, i32, vp, i64, vp, vp, vp, vp, vp, i64, vp]),
+    "kb_device_error_status": (i32, [i32]),
     "kb_gemm": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, vp]),
     "kb_model_create": (i32, [C.POINTER(ModelDesc), C.POINTER(vp)]),
     "kb_model_destroy": (None, [vp]),

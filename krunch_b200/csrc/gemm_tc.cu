@@ -1,0 +1,354 @@
+// tcgen05 GEMM for sm_100a: out[M,N] = epi(A[M,K] @ W[N,K]^T), fp16 in,
+// fp32 accumulation in TMEM, fused RWKV epilogues.
+//
+// Persistent, warp-specialised CTA (one per SM):
+//   warp 0      TMA producer: A 128x64 and W 256x64 tiles (128-byte swizzle)
+//               into a 4-stage shared-memory ring, no cluster multicast;
+//   warp 1      MMA issuer: 4 x tcgen05.mma 128x256x16 per stage into one of
+//               two TMEM accumulators (2 x 256 fp32 columns);
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, the fused
+//               epilogue, 16-byte stores; draining accumulator i overlaps
+//               the MMAs of tile i+1.
+// Output tile (m, n) walks K from 0 to K in 64-wide blocks, 16 per MMA, for
+// every M: a row's result does not depend on M or on the other rows (the
+// M-invariance the decoder relies on, krunch_ac/cuda/det_matmul_tc*.cu).
+// Every mbarrier wait is bounded; on expiry the CTA records an error code in
+// g_tc_error, stops issuing work, frees its TMEM and returns.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "rwkv_ops.cuh"
+#include "tc_common.cuh"
+
+namespace kb {
+
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4, TC_NT = 192;
+constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;          // 16 KB
+constexpr uint32_t TC_B_BYTES = TC_BN * TC_BK * 2;          // 32 KB
+constexpr uint32_t TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;  // 48 KB
+constexpr uint32_t TC_TMEM_COLS = 2 * TC_BN;                // two accumulators
+constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+constexpr uint32_t TC_IDESC = tc::idesc_f16(TC_BM, TC_BN, false);
+
+__device__ int g_tc_error = 0;
+
+struct TcBars {
+    uint64_t full[TC_STAGES];
+    uint64_t empty[TC_STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ void tc_fail(TcBars* b, int code) {
+    atomicExch(&g_tc_error, code);
+    *reinterpret_cast<volatile int*>(&b->abort) = 1;
+}
+__device__ __forceinline__ bool tc_aborted(TcBars* b) {
+    return *reinterpret_cast<volatile int*>(&b->abort) != 0;
+}
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// Epilogue on 32 consecutive columns [c0, c0+32) of row r.
+template <int EPI>
+__device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* out, int64_t ldo,
+                                             const uint16_t* resid, const uint16_t* gate,
+                                             int64_t r, int c0) {
+    const int64_t o = r * ldo + c0;
+    if (EPI == KB_EPI_F32) {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(u2f(acc[4 * j]), u2f(acc[4 * j + 1]), u2f(acc[4 * j + 2]),
+                                 u2f(acc[4 * j + 3]));
+        return;
+    }
+    uint4 rv[4], gv[4];
+    if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID) {
+        const uint4* rs = reinterpret_cast<const uint4*>(resid + o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) rv[j] = rs[j];
+    }
+    if (EPI == KB_EPI_GATE_RESID) {
+        const uint4* gs = reinterpret_cast<const uint4*>(gate + o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) gv[j] = gs[j];
+    }
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t w[4];
+        const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
+        const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv[j]);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float y0 = u2f(acc[8 * j + 2 * h]), y1 = u2f(acc[8 * j + 2 * h + 1]);
+            if (EPI == KB_EPI_SIGMOID) {
+                y0 = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-y0)));
+                y1 = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-y1)));
+            } else if (EPI == KB_EPI_RELU_SQ) {
+                y0 = fmaxf(y0, 0.0f);
+                y1 = fmaxf(y1, 0.0f);
+                y0 = __fmul_rn(y0, y0);
+                y1 = __fmul_rn(y1, y1);
+            } else if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID) {
+                const __half2 rr = *reinterpret_cast<const __half2*>(&rw[h]);
+                float g0 = 1.0f, g1 = 1.0f;
+                if (EPI == KB_EPI_GATE_RESID) {
+                    const __half2 gg = *reinterpret_cast<const __half2*>(&gw[h]);
+                    g0 = __low2float(gg);
+                    g1 = __high2float(gg);
+                }
+                y0 = __fmaf_rn(g0, y0, __low2float(rr));
+                y1 = __fmaf_rn(g1, y1, __high2float(rr));
+            }
+            const __half2 p = __floats2half2_rn(y0, y1);
+            w[h] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_NT, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+              int M, int N, int K, void* out, int64_t ldo, const uint16_t* resid,
+              const uint16_t* gate) {
+    extern __shared__ unsigned char tc_smem_raw[];
+    const uint32_t raw = tc::smem_addr(tc_smem_raw);
+    unsigned char* smem = tc_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    TcBars* bars = reinterpret_cast<TcBars*>(smem + TC_STAGES * TC_STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_n = (N + TC_BN - 1) / TC_BN;
+    const int tiles = ((M + TC_BM - 1) / TC_BM) * num_n;
+    const int KB = K / TC_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            tc::mbar_init(&bars->full[s], 1);
+            tc::mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            tc::mbar_init(&bars->tfull[a], 1);
+            tc::mbar_init(&bars->tempty[a], 4);
+        }
+        bars->abort = 0;
+        tc::fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tc::prefetch_tmap(&mapA);
+        tc::prefetch_tmap(&mapB);
+    }
+    if (warp == 1) tc::tmem_alloc(&bars->tmem_base, TC_TMEM_COLS);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0, issued_parity = 0;  // per-stage bit masks
+            for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x) {
+                const int m0 = (t / num_n) * TC_BM, n0 = (t % num_n) * TC_BN;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1u)) {
+                        tc_fail(bars, 1);
+                        break;
+                    }
+                    unsigned char* sa = smem + stage * TC_STAGE_BYTES;
+                    tc::mbar_expect_tx(&bars->full[stage], TC_STAGE_BYTES);
+                    tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * TC_BK, m0);
+                    tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * TC_BK, n0);
+                    issued |= 1u << stage;
+                    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == TC_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Drain: every load this thread issued has landed before the CTA
+            // exits (immediate on the normal path; bounded after an abort).
+            for (int s = 0; s < TC_STAGES; ++s)
+                if (issued & (1u << s)) tc::mbar_wait(&bars->full[s], (issued_parity >> s) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int i = 0;
+            for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
+                const int a = i & 1;
+                const uint32_t use = (uint32_t)(i >> 1);
+                if (!tc::mbar_wait(&bars->tempty[a], (use & 1u) ^ 1u)) {
+                    tc_fail(bars, 2);
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t d = tmem + (uint32_t)(a * TC_BN);
+                bool ok = true;
+                for (int kb = 0; kb < KB; ++kb) {
+                    if (!tc::mbar_wait(&bars->full[stage], phase)) {
+                        tc_fail(bars, 3);
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t sa = tc::smem_addr(smem + stage * TC_STAGE_BYTES);
+                    const uint32_t sb = sa + TC_A_BYTES;
+#pragma unroll
+                    for (int j = 0; j < TC_BK / 16; ++j)
+                        tc::mma_f16(d, tc::sdesc_k128(sa + 32u * j), tc::sdesc_k128(sb + 32u * j),
+                                    TC_IDESC, (kb | j) != 0);
+                    tc::mma_commit(&bars->empty[stage]);
+                    if (++stage == TC_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc::mma_commit(&bars->tfull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
+            const int a = i & 1;
+            const uint32_t use = (uint32_t)(i >> 1);
+            const int m0 = (t / num_n) * TC_BM, n0 = (t % num_n) * TC_BN;
+            if (!tc::mbar_wait(&bars->tfull[a], use & 1u)) {
+                tc_fail(bars, 4);
+                break;
+            }
+            tc::fence_after_sync();
+            const int64_t row = m0 + q * 32 + lane;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * TC_BN);
+#pragma unroll 1
+            for (int c = 0; c < TC_BN / 32; ++c) {
+                const int col0 = n0 + c * 32;
+                if (col0 >= N) break;
+                uint32_t v[32];
+                tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                tc::tmem_ld_wait();
+                if (row < M) tc_epi_store<EPI>(v, out, ldo, resid, gate, row, col0);
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bars->tempty[a]);
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// Row-major [rows, cols] fp16 with row stride ld (elements), boxed
+// box_rows x 64 with the 128-byte swizzle; out-of-range rows read as zero.
+bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+    static int cache[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+template <int EPI>
+int launch_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N, int K,
+              void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
+              cudaStream_t st) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)TC_SMEM);
+    });
+    if (attr_err != cudaSuccess) {
+        set_cuda_error(attr_err);
+        return KB_ERR_CUDA;
+    }
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, A, M, K, lda, TC_BM) || !make_map(&mb, W, N, K, ldw, TC_BN))
+        return KB_ERR_UNSUPPORTED;
+    const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+    const int grid = tiles < sm_count() ? tiles : sm_count();
+    k_gemm_tc<EPI><<<grid, TC_NT, TC_SMEM, st>>>(ma, mb, M, N, K, out, ldo, resid, gate);
+    return launch_status();
+}
+
+}  // namespace
+
+int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
+                   int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
+                   const uint16_t* gate, cudaStream_t st) {
+    if (M == 0) return KB_OK;
+    switch (epi) {
+        case KB_EPI_F32: return launch_tc<KB_EPI_F32>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        case KB_EPI_F16: return launch_tc<KB_EPI_F16>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        case KB_EPI_SIGMOID: return launch_tc<KB_EPI_SIGMOID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        case KB_EPI_RELU_SQ: return launch_tc<KB_EPI_RELU_SQ>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        case KB_EPI_RESID: return launch_tc<KB_EPI_RESID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
+        default: return KB_ERR_ARG;
+    }
+}
+
+int read_tc_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_tc_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_tc_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace kb

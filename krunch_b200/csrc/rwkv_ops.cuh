@@ -27,4 +27,10 @@ int launch_gemm_f16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t l
                     int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
                     const uint16_t* gate, cudaStream_t st);
 
+int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
+                   int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
+                   const uint16_t* gate, cudaStream_t st);
+// Device-side error code of the tcgen05 kernels (0 = none); optionally reset.
+int read_tc_error(int reset);
+
 }  // namespace kb
