@@ -66,8 +66,19 @@ __global__ void k_encode_lohi(const uint32_t* __restrict__ lohi, int B, int T,
     BitWriter w;
     w.open(out + off, lim, s4[3]);
     const uint2* p = reinterpret_cast<const uint2*>(lohi) + (int64_t)b * T;
-    for (int t = 0; t < n; ++t) {
-        const uint2 iv = p[t];
+    // Intervals are fetched 16 at a time into registers so that the loads of
+    // a block are in flight together instead of one per symbol.
+    constexpr int BLK = 16;
+    int t = 0;
+    for (; t + BLK <= n; t += BLK) {
+        uint2 iv[BLK];
+#pragma unroll
+        for (int j = 0; j < BLK; ++j) iv[j] = __ldg(p + t + j);
+#pragma unroll
+        for (int j = 0; j < BLK; ++j) enc_symbol(e, w, iv[j].x, iv[j].y, bits);
+    }
+    for (; t < n; ++t) {
+        const uint2 iv = __ldg(p + t);
         enc_symbol(e, w, iv.x, iv.y, bits);
     }
     w.close();
@@ -102,7 +113,7 @@ __global__ void k_decode_init(const uint8_t* in, int64_t in_bytes,
     stream_window(in_bytes, offs, b, off, lim);
     BitReader r{in + off, lim, 0u};
     uint32_t v = 0;
-    for (int i = 0; i < 32; ++i) v = (v << 1) | r.get();
+    v = r.get(32);
     uint32_t* s4 = st + 4 * b;
     s4[0] = 0u;
     s4[1] = 0xFFFFFFFFu;

@@ -14,45 +14,49 @@ namespace kb {
 // ----------------------------------------------------------------------------
 // Bit I/O
 // ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t low_mask(int n) { return n >= 32 ? 0xFFFFFFFFu : ((1u << n) - 1u); }
+
 struct BitWriter {
     uint8_t* base;       // stream base
     int64_t limit;       // bytes writable from base (<= 0: nothing writable)
     uint32_t bit_offset; // absolute bit position inside the stream
-    uint32_t acc;        // bits of the current partial byte (right-aligned)
-    int nb;              // number of bits in acc
+    int64_t byte_pos;    // first byte not yet stored
+    uint64_t acc;        // pending bits, right-aligned
+    int nb;              // number of pending bits (< 8 between calls)
 
     __device__ void open(uint8_t* b, int64_t lim, uint32_t off) {
         base = b;
         limit = lim;
         bit_offset = off;
+        byte_pos = off >> 3;
         nb = (int)(off & 7u);
-        const int64_t byte = off >> 3;
-        acc = (nb && byte < limit) ? (uint32_t)(base[byte] >> (8 - nb)) : 0u;
+        acc = (nb && byte_pos < limit) ? (uint64_t)(base[byte_pos] >> (8 - nb)) : 0u;
     }
-    __device__ __forceinline__ void put(uint32_t bit) {
-        acc = (acc << 1) | (bit & 1u);
-        ++nb;
-        ++bit_offset;
-        if (nb == 8) {
-            const int64_t byte = (int64_t)((bit_offset - 1) >> 3);
-            if (byte < limit) base[byte] = (uint8_t)acc;
-            acc = 0;
-            nb = 0;
+    // Append the low n (<= 32) bits of v, most significant first.
+    __device__ __forceinline__ void put(uint32_t v, int n) {
+        acc = (acc << n) | (uint64_t)(v & low_mask(n));
+        nb += n;
+        bit_offset += (uint32_t)n;
+        while (nb >= 8) {
+            nb -= 8;
+            if (byte_pos < limit) base[byte_pos] = (uint8_t)(acc >> nb);
+            ++byte_pos;
         }
     }
-    // Emit `bit` followed by `pending` copies of its complement
+    // `bit` followed by `pending` copies of its complement
     // (cpu_reference._emit, cpu_reference.py:150-154).
     __device__ __forceinline__ void emit(uint32_t bit, uint32_t pending) {
-        put(bit);
-        const uint32_t inv = bit ^ 1u;
-        for (uint32_t i = 0; i < pending; ++i) put(inv);
+        put(bit, 1);
+        const uint32_t fill = bit ? 0u : 0xFFFFFFFFu;
+        while (pending >= 32) {
+            put(fill, 32);
+            pending -= 32;
+        }
+        if (pending) put(fill, (int)pending);
     }
     // Store the trailing partial byte, zero-padded on the right.
     __device__ void close() {
-        if (nb) {
-            const int64_t byte = (int64_t)(bit_offset >> 3);
-            if (byte < limit) base[byte] = (uint8_t)(acc << (8 - nb));
-        }
+        if (nb && byte_pos < limit) base[byte_pos] = (uint8_t)(acc << (8 - nb));
     }
 };
 
@@ -61,17 +65,26 @@ struct BitReader {
     int64_t limit;
     uint32_t bit_offset;
 
-    __device__ __forceinline__ uint32_t get() {
-        const int64_t byte = (int64_t)(bit_offset >> 3);
-        const uint32_t sh = 7u - (bit_offset & 7u);
-        ++bit_offset;
-        if (byte >= limit) return 0u;  // past the buffer: zero bits
-        return (uint32_t)(base[byte] >> sh) & 1u;
+    __device__ __forceinline__ uint32_t byte_at(int64_t i) const {
+        return i < limit ? (uint32_t)base[i] : 0u;  // past the buffer: zero bits
+    }
+    // Next n (1..32) bits, most significant first.
+    __device__ __forceinline__ uint32_t get(int n) {
+        const int64_t b = bit_offset >> 3;
+        const int sh = (int)(bit_offset & 7u);
+        uint64_t w = ((uint64_t)byte_at(b) << 32) | (byte_at(b + 1) << 24) | (byte_at(b + 2) << 16) |
+                     (byte_at(b + 3) << 8) | byte_at(b + 4);
+        bit_offset += (uint32_t)n;
+        return (uint32_t)((w << sh) >> (40 - n)) & low_mask(n);
     }
 };
 
 // ----------------------------------------------------------------------------
-// Encoder / decoder steps
+// Encoder / decoder steps.  Renormalisation moves whole runs at once: the n
+// leading bits on which low and high agree are the n E1/E2 steps of the
+// reference loop, and the following run of straddling bits (low = 01..1,
+// high = 10..0) is its E3 steps; no E1/E2 step can follow an E3 step, so one
+// pass of each reproduces the reference's loop exactly.
 // ----------------------------------------------------------------------------
 struct Enc {
     uint32_t low, high, pending;
@@ -82,24 +95,20 @@ __device__ __forceinline__ void enc_symbol(Enc& s, BitWriter& w, uint32_t lo, ui
     const uint64_t rng = (uint64_t)(s.high - s.low) + 1ull;
     s.high = s.low + (uint32_t)((rng * (uint64_t)hi) >> bits) - 1u;
     s.low = s.low + (uint32_t)((rng * (uint64_t)lo) >> bits);
-    for (;;) {
-        if (s.high < RC_HALF) {
-            w.emit(0u, s.pending);
-            s.pending = 0;
-            s.low <<= 1;
-            s.high = (s.high << 1) | 1u;
-        } else if (s.low >= RC_HALF) {
-            w.emit(1u, s.pending);
-            s.pending = 0;
-            s.low = (s.low - RC_HALF) << 1;
-            s.high = ((s.high - RC_HALF) << 1) | 1u;
-        } else if (s.low >= RC_QTR && s.high < RC_THREE_QTR) {
-            ++s.pending;
-            s.low = (s.low - RC_QTR) << 1;
-            s.high = ((s.high - RC_QTR) << 1) | 1u;
-        } else {
-            break;
-        }
+    const int n = __clz(s.low ^ s.high);  // E1/E2 steps (high > low, so n < 32)
+    if (n > 0) {
+        const uint32_t top = s.low >> (32 - n);
+        w.emit(top >> (n - 1), s.pending);
+        if (n > 1) w.put(top, n - 1);
+        s.pending = 0;
+        s.low <<= n;
+        s.high = (s.high << n) | low_mask(n);
+    }
+    if (s.low >= RC_QTR && s.high < RC_THREE_QTR) {  // E3 steps
+        const int k = min(__clz(~(s.low << 1)), __clz(s.high << 1));
+        s.pending += (uint32_t)k;
+        s.low = (s.low << k) & 0x7FFFFFFFu;
+        s.high = (s.high << k) | 0x80000000u | low_mask(k);
     }
 }
 
@@ -119,22 +128,18 @@ __device__ __forceinline__ void dec_narrow(Dec& s, BitReader& r, uint32_t lo, ui
     const uint64_t rng = (uint64_t)(s.high - s.low) + 1ull;
     s.high = s.low + (uint32_t)((rng * (uint64_t)hi) >> bits) - 1u;
     s.low = s.low + (uint32_t)((rng * (uint64_t)lo) >> bits);
-    for (;;) {
-        if (s.high < RC_HALF) {
-        } else if (s.low >= RC_HALF) {
-            s.low -= RC_HALF;
-            s.high -= RC_HALF;
-            s.value -= RC_HALF;
-        } else if (s.low >= RC_QTR && s.high < RC_THREE_QTR) {
-            s.low -= RC_QTR;
-            s.high -= RC_QTR;
-            s.value -= RC_QTR;
-        } else {
-            break;
-        }
-        s.low <<= 1;
-        s.high = (s.high << 1) | 1u;
-        s.value = (s.value << 1) | r.get();
+    const int n = __clz(s.low ^ s.high);
+    if (n > 0) {
+        s.low <<= n;
+        s.high = (s.high << n) | low_mask(n);
+        s.value = (s.value << n) | r.get(n);
+    }
+    if (s.low >= RC_QTR && s.high < RC_THREE_QTR) {
+        // k E3 steps: x -> ((x - QTR) << 1) | bit, i.e. ((x << k) ^ HALF) | next bits
+        const int k = min(__clz(~(s.low << 1)), __clz(s.high << 1));
+        s.low = (s.low << k) & 0x7FFFFFFFu;
+        s.high = (s.high << k) | 0x80000000u | low_mask(k);
+        s.value = ((s.value << k) ^ 0x80000000u) | r.get(k);
     }
 }
 

@@ -1,7 +1,7 @@
 // RWKV-4 row-local and recurrent kernels: embedding gather, LayerNorm fused
 // with the token-shift mix, the WKV recurrence, decay preparation, state init.
 //
-// Row-local maths is fixed by the row alone (fixed block size, fixed
+// Row-local maths is fixed by the row alone (one warp per row, fixed
 // reduction tree), and the token-shift input of the first row of a window is
 // the carried state, so a window of T rows produces exactly the bits of T
 // single-row steps.  That is what lets the stepped decoder reproduce the
@@ -11,125 +11,154 @@
 
 namespace kb {
 
-constexpr int LN_NT = 256;          // fixed: part of the reduction order
-constexpr float LN_EPS = 1e-5f;     // F.layer_norm default (rwkv4_step_ref.py:57)
+constexpr float LN_EPS = 1e-5f;  // F.layer_norm default (rwkv4_step_ref.py:57)
+constexpr int LN_WARPS = 8;      // warps (rows) per block
 
-__device__ __forceinline__ float ln_block_sum(float v, float* red) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+// One warp per row: lane l owns the EPL = C/32 elements
+//   vector layout (EPL % 8 == 0): 8-element chunks j*32 + l, j < EPL/8
+//   scalar layout (otherwise):    elements j*32 + l,       j < EPL
+// Sums run over the lane's elements in j order, then a xor butterfly — a
+// fixed order, so a row's LayerNorm is the same in every launch shape.
+template <int EPL>
+struct RowIdx {
+    static constexpr bool VEC = (EPL % 8) == 0;
+    __device__ __forceinline__ static int col(int lane, int e) {
+        return VEC ? (((e >> 3) * 32 + lane) << 3) + (e & 7) : e * 32 + lane;
+    }
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-    if (lane == 0) red[w] = v;
-    __syncthreads();
-    float x = (lane < LN_NT / 32) ? red[lane] : 0.0f;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, off));
-    __syncthreads();
-    return x;
+    return v;
 }
 
-// LayerNorm of one row into registers, rounded to fp16 precision (the
-// reference keeps xx in the fp16 activation dtype, rwkv4_step_ref.py:57-61).
-template <int LN_EPT>
-__device__ __forceinline__ void ln_row(const uint16_t* __restrict__ x, int C,
-                                       const float* __restrict__ w, const float* __restrict__ b,
-                                       float* red, float (&out)[LN_EPT]) {
-    const int tid = threadIdx.x;
-    float v[LN_EPT];
-    float s = 0.0f;
+template <int EPL>
+__device__ __forceinline__ void load_vec_f32(const float* __restrict__ p, int lane, float (&v)[EPL]) {
+    if (RowIdx<EPL>::VEC) {
 #pragma unroll
-    for (int j = 0; j < LN_EPT; ++j) {
-        const int c = j * LN_NT + tid;
-        v[j] = (c < C) ? h2f(x[c]) : 0.0f;
-        s = __fadd_rn(s, v[j]);
-    }
-    const float mean = __fdiv_rn(ln_block_sum(s, red), (float)C);
-    float q = 0.0f;
-#pragma unroll
-    for (int j = 0; j < LN_EPT; ++j) {
-        const int c = j * LN_NT + tid;
-        const float d = (c < C) ? __fsub_rn(v[j], mean) : 0.0f;
-        q = __fmaf_rn(d, d, q);
-    }
-    const float var = __fdiv_rn(ln_block_sum(q, red), (float)C);
-    const float rstd = __frsqrt_rn(__fadd_rn(var, LN_EPS));
-#pragma unroll
-    for (int j = 0; j < LN_EPT; ++j) {
-        const int c = j * LN_NT + tid;
-        if (c < C) {
-            const float y = __fmaf_rn(__fmul_rn(__fsub_rn(v[j], mean), rstd), w[c], b[c]);
-            out[j] = __half2float(__float2half_rn(y));
-        } else {
-            out[j] = 0.0f;
-        }
-    }
-}
-
-// LN + token-shift mix over a run of rows of one stream.
-//   grid = (ceil(T / rows_per_cta), B); row index = b*T + t.
-//   prev(t0) = state_in[b] if t0 == 0 else LN(x[t0-1]) (recomputed).
-//   mix_j = xx * m_j + prev * (1 - m_j)   (rwkv4_step_ref.py:59-61)
-// The last row's xx goes to state_out[b].  xx_out (optional) receives xx.
-template <int NMIX, int LN_EPT>
-__global__ void __launch_bounds__(LN_NT) k_ln_mix(const uint16_t* __restrict__ x, int T, int C,
-                                                  int rows_per_cta, const float* __restrict__ lw,
-                                                  const float* __restrict__ lb, MixArgs ma,
-                                                  const float* __restrict__ state_in,
-                                                  float* __restrict__ state_out,
-                                                  uint16_t* __restrict__ xx_out) {
-    __shared__ float red[LN_NT / 32];
-    const int b = blockIdx.y;
-    const int t0 = blockIdx.x * rows_per_cta;
-    if (t0 >= T) return;
-    const int t1 = min(t0 + rows_per_cta, T);
-    const int tid = threadIdx.x;
-    const int64_t row0 = (int64_t)b * T;
-
-    float prev[LN_EPT], cur[LN_EPT];
-    if (NMIX == 0) {
-#pragma unroll
-        for (int j = 0; j < LN_EPT; ++j) prev[j] = 0.0f;
-    } else if (t0 == 0) {
-#pragma unroll
-        for (int j = 0; j < LN_EPT; ++j) {
-            const int c = j * LN_NT + tid;
-            prev[j] = (c < C && state_in) ? state_in[(int64_t)b * C + c] : 0.0f;
+        for (int j = 0; j < EPL / 8; ++j) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(p) + (j * 32 + lane) * 2);
+            const float4 b = __ldg(reinterpret_cast<const float4*>(p) + (j * 32 + lane) * 2 + 1);
+            v[j * 8 + 0] = a.x; v[j * 8 + 1] = a.y; v[j * 8 + 2] = a.z; v[j * 8 + 3] = a.w;
+            v[j * 8 + 4] = b.x; v[j * 8 + 5] = b.y; v[j * 8 + 6] = b.z; v[j * 8 + 7] = b.w;
         }
     } else {
-        ln_row(x + (row0 + t0 - 1) * C, C, lw, lb, red, prev);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) v[e] = __ldg(p + e * 32 + lane);
     }
-    float mk[NMIX > 0 ? NMIX : 1][LN_EPT];
-#pragma unroll
-    for (int m = 0; m < NMIX; ++m)
-#pragma unroll
-        for (int j = 0; j < LN_EPT; ++j) {
-            const int c = j * LN_NT + tid;
-            mk[m][j] = (c < C) ? ma.mix[m][c] : 0.0f;
-        }
+}
 
-    for (int t = t0; t < t1; ++t) {
-        const int64_t row = row0 + t;
-        ln_row(x + row * C, C, lw, lb, red, cur);
+template <int EPL>
+__device__ __forceinline__ void load_row(const uint16_t* __restrict__ x, int lane, float (&v)[EPL]) {
+    if (RowIdx<EPL>::VEC) {
 #pragma unroll
-        for (int j = 0; j < LN_EPT; ++j) {
-            const int c = j * LN_NT + tid;
-            if (c < C) {
-                if (xx_out) xx_out[row * C + c] = f2h(cur[j]);
+        for (int j = 0; j < EPL / 8; ++j) {
+            const uint4 q = __ldg(reinterpret_cast<const uint4*>(x) + j * 32 + lane);
+            const __half2* h = reinterpret_cast<const __half2*>(&q);
 #pragma unroll
-                for (int m = 0; m < NMIX; ++m) {
-                    const float one_m = __fsub_rn(1.0f, mk[m][j]);
-                    const float y = __fmaf_rn(cur[j], mk[m][j], __fmul_rn(prev[j], one_m));
-                    ma.out[m][row * C + c] = f2h(y);
-                }
-            }
-            prev[j] = cur[j];
-        }
-        if (t == T - 1 && state_out) {
-#pragma unroll
-            for (int j = 0; j < LN_EPT; ++j) {
-                const int c = j * LN_NT + tid;
-                if (c < C) state_out[(int64_t)b * C + c] = cur[j];
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __half22float2(h[k]);
+                v[j * 8 + 2 * k] = f.x;
+                v[j * 8 + 2 * k + 1] = f.y;
             }
         }
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) v[e] = h2f(x[e * 32 + lane]);
+    }
+}
+
+// LayerNorm of one row (values in v), result rounded to fp16 precision (the
+// reference keeps xx in the fp16 activation dtype, rwkv4_step_ref.py:57-61).
+template <int EPL>
+__device__ __forceinline__ void ln_warp(const float (&v)[EPL], int C, int lane,
+                                        const float* __restrict__ w, const float* __restrict__ b,
+                                        float (&out)[EPL]) {
+    float s = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s = __fadd_rn(s, v[e]);
+    const float mean = __fdiv_rn(warp_sum(s), (float)C);
+    float q = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const float d = __fsub_rn(v[e], mean);
+        q = __fmaf_rn(d, d, q);
+    }
+    const float rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(q), (float)C), LN_EPS));
+    float wv[EPL], bv[EPL];
+    load_vec_f32<EPL>(w, lane, wv);
+    load_vec_f32<EPL>(b, lane, bv);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        const float y = __fmaf_rn(__fmul_rn(__fsub_rn(v[e], mean), rstd), wv[e], bv[e]);
+        out[e] = __half2float(__float2half_rn(y));
+    }
+}
+
+template <int EPL>
+__device__ __forceinline__ void store_row_f16(uint16_t* __restrict__ dst, int lane, const float (&v)[EPL]) {
+    if (RowIdx<EPL>::VEC) {
+#pragma unroll
+        for (int j = 0; j < EPL / 8; ++j) {
+            uint4 q;
+            __half2* h = reinterpret_cast<__half2*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[j * 8 + 2 * k], v[j * 8 + 2 * k + 1]);
+            reinterpret_cast<uint4*>(dst)[j * 32 + lane] = q;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e * 32 + lane] = f2h(v[e]);
+    }
+}
+
+// LN + token-shift mix, one warp per row, every row independent:
+//   prev(t) = state_in[b] for t == 0, else LN(x[t-1]) recomputed by this warp
+//   mix_j   = xx * m_j + prev * (1 - m_j)   (rwkv4_step_ref.py:59-61)
+// Row index = b*T + t.  The stream's last row writes its xx to state_out[b];
+// xx_out (optional) receives xx.
+template <int NMIX, int EPL>
+__global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __restrict__ x, int B,
+                                                          int T, int C,
+                                                          const float* __restrict__ lw,
+                                                          const float* __restrict__ lb, MixArgs ma,
+                                                          const float* __restrict__ state_in,
+                                                          float* __restrict__ state_out,
+                                                          uint16_t* __restrict__ xx_out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
+    if (row >= (int64_t)B * T) return;
+    const int b = (int)(row / T);
+    const int t = (int)(row - (int64_t)b * T);
+
+    float v[EPL], cur[EPL], prev[EPL];
+    load_row<EPL>(x + row * C, lane, v);
+    if (NMIX > 0) {
+        if (t == 0) {
+#pragma unroll
+            for (int e = 0; e < EPL; ++e)
+                prev[e] = state_in ? state_in[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] : 0.0f;
+        } else {
+            float pv[EPL];
+            load_row<EPL>(x + (row - 1) * C, lane, pv);
+            ln_warp<EPL>(pv, C, lane, lw, lb, prev);
+        }
+    }
+    ln_warp<EPL>(v, C, lane, lw, lb, cur);
+    if (xx_out) store_row_f16<EPL>(xx_out + row * C, lane, cur);
+#pragma unroll
+    for (int m = 0; m < NMIX; ++m) {
+        float mk[EPL];
+        load_vec_f32<EPL>(ma.mix[m], lane, mk);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e)
+            mk[e] = __fmaf_rn(cur[e], mk[e], __fmul_rn(prev[e], __fsub_rn(1.0f, mk[e])));
+        store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
+    }
+    if (t == T - 1 && state_out) {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) state_out[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] = cur[e];
     }
 }
 
@@ -142,14 +171,45 @@ __global__ void __launch_bounds__(LN_NT) k_ln_mix(const uint16_t* __restrict__ x
 //   ww2 = pp - decay; p2 = max(ww2, k); aa = e^(ww2-p2)*aa + e^(k-p2)*v;
 //   bb = e^(ww2-p2)*bb + e^(k-p2); pp = p2.
 // Output ry = r * y in fp16 (the (r * y) @ Ow operand, rwkv4_step_ref.py:96).
+// Loads are issued WKV_BLK time steps at a time; every operation is an
+// explicit intrinsic, so the blocked loop and the one-step tail (the stepped
+// decoder, T = 1) compute identical bits.
+constexpr int WKV_BLK = 16;
+
 template <int CONV>
-__global__ void __launch_bounds__(128) k_wkv(int B, int T, int C, const float* __restrict__ k,
-                                             const float* __restrict__ v,
-                                             const uint16_t* __restrict__ r,
-                                             const float* __restrict__ decay,
-                                             const float* __restrict__ first, float* aa_s,
-                                             float* bb_s, float* pp_s,
-                                             uint16_t* __restrict__ ry) {
+__device__ __forceinline__ float wkv_step(float& aa, float& bb, float& pp, float kt, float vt,
+                                          float u, float dec) {
+    float e1, e2;
+    if (CONV == KB_WKV_STEP_REF) {
+        const float ww = __fadd_rn(pp, u);
+        const float p = fmaxf(ww, kt);
+        e1 = __expf(__fsub_rn(ww, p));
+        e2 = __expf(__fsub_rn(kt, p));
+    } else {
+        const float ww = __fadd_rn(u, kt);
+        const float p = fmaxf(pp, ww);
+        e1 = __expf(__fsub_rn(pp, p));
+        e2 = __expf(__fsub_rn(ww, p));
+    }
+    const float y = __fdividef(__fmaf_rn(e1, aa, __fmul_rn(e2, vt)), __fmaf_rn(e1, bb, e2));
+    const float ww2 = __fsub_rn(pp, dec);
+    const float p2 = fmaxf(ww2, kt);
+    const float f1 = __expf(__fsub_rn(ww2, p2));
+    const float f2 = __expf(__fsub_rn(kt, p2));
+    aa = __fmaf_rn(f1, aa, __fmul_rn(f2, vt));
+    bb = __fmaf_rn(f1, bb, f2);
+    pp = p2;
+    return y;
+}
+
+template <int CONV>
+__global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float* __restrict__ k,
+                                                const float* __restrict__ v,
+                                                const uint16_t* __restrict__ r,
+                                                const float* __restrict__ decay,
+                                                const float* __restrict__ first, float* aa_s,
+                                                float* bb_s, float* pp_s,
+                                                uint16_t* __restrict__ ry) {
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= B * C) return;
     const int b = idx / C, c = idx - b * C;
@@ -157,35 +217,37 @@ __global__ void __launch_bounds__(128) k_wkv(int B, int T, int C, const float* _
     const float u = first[c];
     float aa = aa_s[idx], bb = bb_s[idx], pp = pp_s[idx];
     const int64_t base = (int64_t)b * T * C + c;
-#pragma unroll 4
-    for (int t = 0; t < T; ++t) {
-        const int64_t o = base + (int64_t)t * C;
-        const float kt = k[o];
-        const float vt = v[o];
-        const float rt = h2f(r[o]);
-        float e1, e2;
-        if (CONV == KB_WKV_STEP_REF) {
-            const float ww = __fadd_rn(pp, u);
-            const float p = fmaxf(ww, kt);
-            e1 = __expf(__fsub_rn(ww, p));
-            e2 = __expf(__fsub_rn(kt, p));
-        } else {
-            const float ww = __fadd_rn(u, kt);
-            const float p = fmaxf(pp, ww);
-            e1 = __expf(__fsub_rn(pp, p));
-            e2 = __expf(__fsub_rn(ww, p));
+    const float* kp = k + base;
+    const float* vp = v + base;
+    const uint16_t* rp = r + base;
+    uint16_t* op = ry + base;
+    int t0 = 0;
+    for (; t0 + WKV_BLK <= T; t0 += WKV_BLK) {
+        float kb[WKV_BLK], vb[WKV_BLK];
+        uint16_t rb[WKV_BLK];
+#pragma unroll
+        for (int j = 0; j < WKV_BLK; ++j) {
+            kb[j] = __ldg(kp);
+            vb[j] = __ldg(vp);
+            rb[j] = __ldg(rp);
+            kp += C;
+            vp += C;
+            rp += C;
         }
-        const float num = __fmaf_rn(e1, aa, __fmul_rn(e2, vt));
-        const float den = __fmaf_rn(e1, bb, e2);
-        const float y = __fdiv_rn(num, den);
-        ry[o] = f2h(__fmul_rn(rt, y));
-        const float ww2 = __fsub_rn(pp, dec);
-        const float p2 = fmaxf(ww2, kt);
-        const float f1 = __expf(__fsub_rn(ww2, p2));
-        const float f2 = __expf(__fsub_rn(kt, p2));
-        aa = __fmaf_rn(f1, aa, __fmul_rn(f2, vt));
-        bb = __fmaf_rn(f1, bb, f2);
-        pp = p2;
+#pragma unroll
+        for (int j = 0; j < WKV_BLK; ++j) {
+            const float y = wkv_step<CONV>(aa, bb, pp, kb[j], vb[j], u, dec);
+            *op = f2h(__fmul_rn(h2f(rb[j]), y));
+            op += C;
+        }
+    }
+    for (; t0 < T; ++t0) {
+        const float y = wkv_step<CONV>(aa, bb, pp, __ldg(kp), __ldg(vp), u, dec);
+        *op = f2h(__fmul_rn(h2f(__ldg(rp)), y));
+        kp += C;
+        vp += C;
+        rp += C;
+        op += C;
     }
     aa_s[idx] = aa;
     bb_s[idx] = bb;
@@ -235,16 +297,19 @@ int launch_embed(const int32_t* tok, int64_t rows, int V, int C, const uint16_t*
 }
 
 template <int NMIX>
-static void ln_mix_ept(int ept, dim3 grid, cudaStream_t st, const uint16_t* x, int T, int C,
-                       int rpc, const float* lw, const float* lb, const MixArgs& ma,
-                       const float* state_in, float* state_out, uint16_t* xx_out) {
-#define KB_LN_CASE(E)                                                                         \
-    case E:                                                                                   \
-        k_ln_mix<NMIX, E><<<grid, LN_NT, 0, st>>>(x, T, C, rpc, lw, lb, ma, state_in,        \
-                                                   state_out, xx_out);                        \
-        break;
-    switch (ept) {
-        KB_LN_CASE(1) KB_LN_CASE(2) KB_LN_CASE(3) KB_LN_CASE(4) KB_LN_CASE(8) KB_LN_CASE(16)
+static int ln_mix_epl(int epl, int blocks, cudaStream_t st, const uint16_t* x, int B, int T, int C,
+                      const float* lw, const float* lb, const MixArgs& ma, const float* state_in,
+                      float* state_out, uint16_t* xx_out) {
+#define KB_LN_CASE(E)                                                                           \
+    case E:                                                                                     \
+        k_ln_mix<NMIX, E><<<blocks, LN_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in,   \
+                                                            state_out, xx_out);                 \
+        return KB_OK;
+    switch (epl) {
+        KB_LN_CASE(4) KB_LN_CASE(8) KB_LN_CASE(16) KB_LN_CASE(24) KB_LN_CASE(32) KB_LN_CASE(48)
+        KB_LN_CASE(64)
+        default:
+            return KB_ERR_SHAPE;
     }
 #undef KB_LN_CASE
 }
@@ -252,17 +317,18 @@ static void ln_mix_ept(int ept, dim3 grid, cudaStream_t st, const uint16_t* x, i
 int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float* lw,
                   const float* lb, const MixArgs& ma, const float* state_in, float* state_out,
                   uint16_t* xx_out, cudaStream_t st) {
-    const int need = (C + LN_NT - 1) / LN_NT;
-    const int ept = need <= 4 ? need : (need <= 8 ? 8 : 16);
-    if (need > 16) return KB_ERR_SHAPE;
-    const int rpc = T >= 64 ? 16 : (T >= 8 ? 4 : 1);
-    dim3 grid((T + rpc - 1) / rpc, B);
+    if (C % 32) return KB_ERR_SHAPE;
+    const int epl = C / 32;
+    const int64_t rows = (int64_t)B * T;
+    const int blocks = (int)((rows + LN_WARPS - 1) / LN_WARPS);
+    int rc;
     switch (nmix) {
-        case 0: ln_mix_ept<0>(ept, grid, st, x, T, C, rpc, lw, lb, ma, state_in, state_out, xx_out); break;
-        case 2: ln_mix_ept<2>(ept, grid, st, x, T, C, rpc, lw, lb, ma, state_in, state_out, xx_out); break;
-        case 3: ln_mix_ept<3>(ept, grid, st, x, T, C, rpc, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 0: rc = ln_mix_epl<0>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 2: rc = ln_mix_epl<2>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 3: rc = ln_mix_epl<3>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
         default: return KB_ERR_ARG;
     }
+    if (rc != KB_OK) return rc;
     return launch_status();
 }
 
