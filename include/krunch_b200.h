@@ -131,9 +131,16 @@ enum kb_cdf_mode {
                           s = symbols[row]; feeds kb_coder_encode_lohi      */
 };
 
-/* logits fp16 [rows, row_stride] (V valid columns). */
+/* With logit_stats NULL, logits_f16 holds raw fp16 logits [rows, row_stride]
+ * (V valid columns).  With logit_stats non-NULL it holds what
+ * kb_forward_window writes when asked for stats: per 64-column subtile u the
+ * fp16 numerators e^(x - m_u), and logit_stats float2 [rows, stats_stride]
+ * the subtile partials (m_u, sum of the numerators), stats_stride >=
+ * ceil(V / 64).  Both inputs give bit-identical CDFs (the kernel derives the
+ * numerators and partials from raw logits itself). */
 int kb_cdf_rows(const uint16_t* logits_f16, int64_t row_stride, int rows, int V,
-                int cdf_bits, int mode, const int32_t* symbols, void* out, void* stream);
+                int cdf_bits, int mode, const float* logit_stats, int64_t stats_stride,
+                const int32_t* symbols, void* out, void* stream);
 
 /* probs fp32 [rows, V] -> int32 CDF [rows, V+1].  Replaces probs_to_cdf_gpu
  * (krunch_ac/gpu_encode.py:22-48) with a fixed-order row reduction. */
@@ -151,10 +158,10 @@ int kb_cdf_from_probs(const float* probs, int rows, int V, int cdf_bits, int32_t
  * history[b * hist_stride + counters[b][0]].  All pointers stay fixed from
  * step to step, so a decode step can be captured in a CUDA graph. */
 int kb_decode_logits_step(const uint16_t* logits_f16, int64_t row_stride, int B, int V,
-                          int cdf_bits, const uint8_t* in, int64_t in_bytes,
-                          const int64_t* in_offsets, uint32_t* states, int32_t* counters,
-                          int32_t* out_syms, int32_t* history, int64_t hist_stride,
-                          void* stream);
+                          int cdf_bits, const float* logit_stats, int64_t stats_stride,
+                          const uint8_t* in, int64_t in_bytes, const int64_t* in_offsets,
+                          uint32_t* states, int32_t* counters, int32_t* out_syms,
+                          int32_t* history, int64_t hist_stride, void* stream);
 
 /* ------------------------------------------------------------------------- */
 /* GEMM: out[M,N] = epilogue(A[M,K] @ W^T) with W stored K-major as [N,K]    */
@@ -237,14 +244,17 @@ int kb_state_init(const kb_model* model, float* state, int B, void* stream);
 size_t kb_forward_workspace_bytes(const kb_model* model, int B, int T);
 
 /* Packed forward of a window: tokens int32 [B, T] (inputs), state as above
- * (read and updated), logits fp16 [B*T, vocab_pad] (row b*T+t).  T = 1 is the
- * stepped decompress forward; the same kernels run for every T, which makes
- * packed and stepped logits bit-identical.  Replaces forward_packed_window /
- * forward_stepped_batched (krunch/cpp_path.py:131-163,428-460) and
- * rwkv4_layer_step_cpp (layer_cpp.cpp:456-637). */
+ * (read and updated), logits fp16 [B*T, vocab_pad] (row b*T+t).  When
+ * logit_stats is non-NULL the head writes, instead of raw logits, the softmax
+ * numerators and partials kb_cdf_rows takes (stats float2 [B*T, vocab_pad/64]).
+ * T = 1 is the stepped decompress forward; the same kernels run for every T,
+ * which makes packed and stepped results bit-identical.  Replaces
+ * forward_packed_window / forward_stepped_batched
+ * (krunch/cpp_path.py:131-163,428-460) and rwkv4_layer_step_cpp
+ * (layer_cpp.cpp:456-637). */
 int kb_forward_window(const kb_model* model, const int32_t* tokens, int B, int T,
                       float* state, void* workspace, size_t workspace_bytes,
-                      uint16_t* logits, void* stream);
+                      uint16_t* logits, float* logit_stats, void* stream);
 
 /* Allocation-free variant of kb_forward_window.  No counterpart in the
  * reference: it exists for hosts that cannot allocate device memory when they

@@ -55,9 +55,9 @@ SIGNATURES = {
     "kb_coder_encode_finalize": (i32, [vp, i64, vp, vp, i32, vp]),
     "kb_coder_decode_init": (i32, [vp, i64, vp, vp, i32, vp]),
     "kb_coder_decode_cdf": (i32, [vp, i64, i32, i32, vp, i64, vp, vp, vp, i32, vp]),
-    "kb_cdf_rows": (i32, [vp, i64, i32, i32, i32, i32, vp, vp, vp]),
+    "kb_cdf_rows": (i32, [vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, vp]),
     "kb_cdf_from_probs": (i32, [vp, i32, i32, i32, vp, vp]),
-    "kb_decode_logits_step": (i32, [vp, i64, i32, i32, i32, vp, i64, vp, vp, vp, vp, vp, i64, vp]),
+    "kb_decode_logits_step": (i32, [vp, i64, i32, i32, i32, vp, i64, vp, i64, vp, vp, vp, vp, vp, i64, vp]),
     "kb_device_error_status": (i32, [i32]),
     "kb_gemm": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, vp]),
     "kb_model_create": (i32, [C.POINTER(ModelDesc), C.POINTER(vp)]),
@@ -65,7 +65,7 @@ SIGNATURES = {
     "kb_prepare_decay": (i32, [vp, vp, i32, vp]),
     "kb_state_init": (i32, [vp, vp, i32, vp]),
     "kb_forward_workspace_bytes": (sz, [vp, i32, i32]),
-    "kb_forward_window": (i32, [vp, vp, i32, i32, vp, vp, sz, vp, vp]),
+    "kb_forward_window": (i32, [vp, vp, i32, i32, vp, vp, sz, vp, vp, vp]),
     "kb_forward_window_noalloc": (i32, [vp, vp, i32, i32, vp, vp, vp]),
 }
 

@@ -92,11 +92,13 @@ class Codec:
         plan.run()
         return plan.fetch()
 
-    def encode_window(self, logits, sym_w, lohi, B, tw, n_valid, out_d, offs_d, ac) -> None:
+    def encode_window(self, logits, stats, sym_w, lohi, B, tw, n_valid, out_d, offs_d,
+                      ac) -> None:
         """(lo, hi) of every row's symbol, then lane-per-stream encode."""
         m, s = self.model, N.stream_ptr(self.dev)
         N.call("kb_cdf_rows", logits.data_ptr(), m.spec.vocab_pad, B * tw, m.spec.n_vocab,
-               self.bits, N.KB_CDF_LOHI, sym_w.data_ptr(), lohi.data_ptr(), s)
+               self.bits, N.KB_CDF_LOHI, stats.data_ptr(), m.stats_stride, sym_w.data_ptr(),
+               lohi.data_ptr(), s)
         N.call("kb_coder_encode_lohi", lohi.data_ptr(), B, tw, n_valid.data_ptr(), self.bits,
                out_d.data_ptr(), out_d.numel(), offs_d.data_ptr(), ac.data_ptr(), s)
 
@@ -146,6 +148,7 @@ class CompressPlan:
         self.state = m.new_state(B)
         self.ws = m.new_workspace(B, self.Tw)
         self.logits = m.new_logits(B, self.Tw)
+        self.stats = m.new_stats(B, self.Tw)
         self.lohi = torch.empty((B, self.Tw, 2), dtype=torch.int32, device=dev)
         self.windows = (Tmax + self.Tw - 1) // self.Tw
         self._pin = torch.empty((2, B, Tmax), dtype=torch.int32).pin_memory()
@@ -186,8 +189,8 @@ class CompressPlan:
             else:
                 tok_w = self.inp_d[:, off:off + tw].contiguous()
                 sym_w = self.tgt_d[:, off:off + tw].contiguous()
-            m.forward_window(tok_w, self.state, self.ws, self.logits)
-            c.encode_window(self.logits, sym_w, self.lohi, self.B, tw,
+            m.forward_window(tok_w, self.state, self.ws, self.logits, self.stats)
+            c.encode_window(self.logits, self.stats, sym_w, self.lohi, self.B, tw,
                             (self.lens_d - off).clamp(0, tw).int(), self.out_d, self.offs_d,
                             self.ac)
         N.call("kb_coder_encode_finalize", self.out_d.data_ptr(), self.total,
@@ -239,6 +242,7 @@ class DecompressPlan:
         self.state = m.new_state(B)
         self.ws = m.new_workspace(B, 1)
         self.logits = m.new_logits(B, 1)
+        self.stats = m.new_stats(B, 1)
         self.graph = None
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -253,9 +257,10 @@ class DecompressPlan:
 
     def _step(self) -> None:
         c, m = self.codec, self.codec.model
-        m.forward_window(self.cur, self.state, self.ws, self.logits)
+        m.forward_window(self.cur, self.state, self.ws, self.logits, self.stats)
         N.call("kb_decode_logits_step", self.logits.data_ptr(), m.spec.vocab_pad, self.B,
-               m.spec.n_vocab, c.bits, self.in_d.data_ptr(), self.nbytes, self.offs_d.data_ptr(),
+               m.spec.n_vocab, c.bits, self.stats.data_ptr(), m.stats_stride, self.in_d.data_ptr(),
+               self.nbytes, self.offs_d.data_ptr(),
                self.ac.data_ptr(), self.counters.data_ptr(), self.cur.data_ptr(),
                self.history.data_ptr(), self.history.shape[1], N.stream_ptr(c.dev))
 

@@ -1,4 +1,4 @@
-// Fused logits -> softmax -> integer CDF, one CTA per row.
+// logits -> softmax -> integer CDF, one CTA per row.
 //
 // Spec (krunch_ac/cdf.py:22-74, krunch_ac/cuda/det_softmax_cdf.cu:62-185):
 //   p_i    = softmax(logits)_i
@@ -6,24 +6,36 @@
 //   c_amax += T - sum(c)                         (argmax of p, smallest index on ties)
 //   cdf    = [0, cumsum(c)]
 //
-// Every float operation of a row happens in an order fixed by V alone:
-// thread t of the CDF_NT-thread block owns the contiguous segment
-// [t*L, min((t+1)*L, V)) with L = ceil(V / CDF_NT), sums it sequentially,
-// and the per-thread partials meet in a fixed xor-butterfly (warp) then a
-// fixed butterfly over the warp partials.  exp is kb_expf (kb_common.cuh).
-// Integer sums are exact, so their order is free.  A row's CDF is therefore
-// bit-identical whatever the number of rows, the launch, or the GPU, and
-// the C restatement in oracle/ reproduces it bit for bit.
+// The softmax follows softmax_stats.cuh: per 64-column subtile u a max m_u
+// and fp16 numerators e_i = e^(x_i - m_u); the only floating-point reduction,
+// the normaliser (M, S), merges the subtile partials in a fixed order.  With
+// gs_u = (e^(m_u - M) / S) * (T - V) a count is c_i = floor(e_i * gs_u) + 1,
+// and the argmax of q_i = e_i * gs_u (smallest index on ties) is the first
+// e_i == 1 in the first subtile with the largest gs_u: every subtile's max has
+// e = 1 exactly, and q_i < gs_u whenever e_i < 1 (the largest fp16 below 1 is
+// 1 - 2^-11), so no per-element comparison is needed.  The head GEMM hands
+// over e_i and the partials; given raw logits the kernel derives both.
+// Everything is explicitly rounded or integer, so a row's CDF is
+// bit-identical for any number of rows, any launch and any GPU, and the C
+// restatement in oracle/ reproduces it bit for bit.
+//
+// Element pass: warp w of 16 owns the contiguous range [w*Lw, (w+1)*Lw)
+// (Lw a multiple of 256); per step each lane takes 8 consecutive values with
+// one 16-byte load.  Ranges are in index order, which gives the decoder its
+// prefix sums.
 //
 // Modes: COUNTS / CDF write [rows, V+1] int32 (reference contract);
 // LOHI writes only the (cdf[s], cdf[s+1]) pair of the row's symbol (the
 // compress hot path — the [rows, V+1] CDF is never materialised);
 // DECODE runs the range-decoder step for stream `row` in the same CTA.
+// The probability-input variant (kb_cdf_from_probs) keeps a per-thread
+// segmented sum (k_cdf_probs).
 #include <float.h>
 #include <limits.h>
 
 #include "coder.cuh"
 #include "profile.cuh"
+#include "softmax_stats.cuh"
 
 namespace kb {
 
@@ -33,6 +45,7 @@ constexpr int MODE_COUNTS = KB_CDF_COUNTS;
 constexpr int MODE_CDF = KB_CDF_CDF;
 constexpr int MODE_LOHI = KB_CDF_LOHI;
 constexpr int MODE_DECODE = 3;
+constexpr int MAX_SUB = 65536 / SUBTILE;
 
 struct CdfRed {
     float f[CDF_NW];
@@ -41,22 +54,8 @@ struct CdfRed {
     int i2[CDF_NW];
 };
 
-__device__ __forceinline__ float block_max_f(float v, CdfRed& r) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
-    if (lane == 0) r.f[w] = v;
-    __syncthreads();
-    float x = (lane < CDF_NW) ? r.f[lane] : -INFINITY;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, off));
-    __syncthreads();
-    return x;
-}
-
 // Fixed-tree float sum: butterfly in each warp, then the same butterfly over
-// the CDF_NW warp partials (zero padded to 32).  IEEE addition commutes, so
-// every lane of a butterfly holds the same value.
+// the CDF_NW warp partials (zero padded to 32).
 __device__ __forceinline__ float block_sum_f(float v, CdfRed& r) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -116,210 +115,326 @@ __device__ __forceinline__ int block_argmax(float v, int i, CdfRed& r) {
     return xi;
 }
 
-// Exclusive prefix sum over threads (integer, exact).
-__device__ __forceinline__ int block_excl_scan_i(int v, CdfRed& r) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    int inc = v;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, off);
-        if (lane >= off) inc += y;
-    }
-    if (lane == 31) r.i[w] = inc;
-    __syncthreads();
-    if (w == 0) {
-        int t = (lane < CDF_NW) ? r.i[lane] : 0;
-        int tinc = t;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, tinc, off);
-            if (lane >= off) tinc += y;
-        }
-        if (lane < CDF_NW) r.i2[lane] = tinc - t;
-    }
-    __syncthreads();
-    const int res = r.i2[w] + inc - v;
-    __syncthreads();
-    return res;
-}
-
-// Copy one fp16 row into shared memory with the widest aligned loads.
-__device__ __forceinline__ void load_row_f16(const uint16_t* __restrict__ x, uint16_t* sx, int V) {
-    const int tid = threadIdx.x;
-    if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
-        const int nv = V >> 3;
-        const uint4* xv = reinterpret_cast<const uint4*>(x);
-        uint4* sv = reinterpret_cast<uint4*>(sx);
-#pragma unroll 4
-        for (int i = tid; i < nv; i += CDF_NT) sv[i] = __ldg(xv + i);
-        for (int i = (nv << 3) + tid; i < V; i += CDF_NT) sx[i] = x[i];
-    } else if ((reinterpret_cast<uintptr_t>(x) & 3u) == 0) {
-        const int nv = V >> 1;
-        const uint32_t* xv = reinterpret_cast<const uint32_t*>(x);
-        uint32_t* sv = reinterpret_cast<uint32_t*>(sx);
-#pragma unroll 4
-        for (int i = tid; i < nv; i += CDF_NT) sv[i] = __ldg(xv + i);
-        for (int i = (nv << 1) + tid; i < V; i += CDF_NT) sx[i] = x[i];
-    } else {
-        for (int i = tid; i < V; i += CDF_NT) sx[i] = x[i];
-    }
-}
-
-// Row source: probability p_i of element i after the normalisation pass.
-struct LogitsRow {
-    const uint16_t* sx;  // shared memory copy of the row
-    float m, inv;
-    __device__ __forceinline__ float p(int i) const {
-        return __fmul_rn(kb_expf(__fsub_rn(h2f(sx[i]), m)), inv);
-    }
-};
-struct ProbsRow {
-    const float* x;  // global row
-    float s;
-    __device__ __forceinline__ float p(int i) const { return __fdiv_rn(x[i], s); }
-};
-
-template <int MODE, bool FROM_PROBS>
-__global__ void __launch_bounds__(CDF_NT) k_cdf(const void* __restrict__ src, int64_t stride,
-                                                int V, int bits,
-                                                const int32_t* __restrict__ symbols, void* out,
-                                                const uint8_t* in, int64_t in_bytes,
-                                                const int64_t* __restrict__ in_offs,
-                                                uint32_t* states, int32_t* counters,
-                                                int32_t* out_syms, int32_t* history,
-                                                int64_t hist_stride) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+// ---------------------------------------------------------------------------
+// probabilities -> CDF (kb_cdf_from_probs): thread t sums its segment
+// [t*L, min((t+1)*L, V)) left to right, partials meet in the fixed butterfly;
+// p_i = x_i / S, c_i = floor(p_i * (T - V)) + 1, argmax over p_i.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(CDF_NT) k_cdf_probs(const float* __restrict__ probs, int V,
+                                                      int bits, int32_t* __restrict__ out) {
     __shared__ CdfRed red;
-    __shared__ int s_csym, s_owner, s_owner_base, s_sym;
-    __shared__ uint32_t s_target, s_lo, s_hi;
-
-    const int row = blockIdx.x;
-    const int tid = threadIdx.x;
-    if (MODE == MODE_DECODE && counters && counters[2 * row] >= counters[2 * row + 1]) {
-        if (tid == 0) out_syms[row] = 0;
-        return;
-    }
+    __shared__ int s_wsum[CDF_NT];
+    const int row = blockIdx.x, tid = threadIdx.x;
     const int L = (V + CDF_NT - 1) / CDF_NT;
-    const int a = min(tid * L, V);
-    const int e = min(a + L, V);
+    const int a = min(tid * L, V), e = min(a + L, V);
     const int T = 1 << bits;
     const float scale = (float)(T - V);
-
-    int sym = 0;
-    if (MODE == MODE_LOHI) {
-        sym = symbols[row];
-        sym = sym < 0 ? 0 : (sym >= V ? V - 1 : sym);
-    }
-    if (MODE == MODE_DECODE && tid == 0) s_target = decode_target(states + 4 * (int64_t)row, bits);
-
-    // ---- normalisation pass ------------------------------------------------
-    LogitsRow lr;
-    ProbsRow pr;
-    if (!FROM_PROBS) {
-        uint16_t* sx = reinterpret_cast<uint16_t*>(smem_raw);
-        load_row_f16(reinterpret_cast<const uint16_t*>(src) + (int64_t)row * stride, sx, V);
-        __syncthreads();
-        float mt = -INFINITY;
-        for (int i = a; i < e; ++i) mt = fmaxf(mt, h2f(sx[i]));
-        const float m = block_max_f(mt, red);
-        float st = 0.0f;
-        for (int i = a; i < e; ++i) st = __fadd_rn(st, kb_expf(__fsub_rn(h2f(sx[i]), m)));
-        const float S = block_sum_f(st, red);
-        lr.sx = sx;
-        lr.m = m;
-        lr.inv = __frcp_rn(S);
-    } else {
-        const float* x = reinterpret_cast<const float*>(src) + (int64_t)row * stride;
-        float st = 0.0f;
-        for (int i = a; i < e; ++i) st = __fadd_rn(st, x[i]);
-        const float S = block_sum_f(st, red);
-        pr.x = x;
-        pr.s = fmaxf(S, 1e-30f);
-    }
-    auto prob = [&](int i) -> float { return FROM_PROBS ? pr.p(i) : lr.p(i); };
-    auto count = [&](float p) -> int { return (int)floorf(__fmul_rn(p, scale)) + 1; };
-
-    // ---- counts, argmax, totals ------------------------------------------
-    int cs = 0, below = 0;
+    const float* x = probs + (int64_t)row * V;
+    float st = 0.0f;
+    for (int i = a; i < e; ++i) st = __fadd_rn(st, x[i]);
+    const float S = fmaxf(block_sum_f(st, red), 1e-30f);
+    int cs = 0;
     float bp = -INFINITY;
     int bi = INT_MAX;
     for (int i = a; i < e; ++i) {
-        const float p = prob(i);
-        const int c = count(p);
-        cs += c;
-        if (p > bp) {  // ascending scan: strict '>' keeps the smallest index
+        const float p = __fdiv_rn(x[i], S);
+        cs += (int)floorf(__fmul_rn(p, scale)) + 1;
+        if (p > bp) {
             bp = p;
             bi = i;
         }
-        if (MODE == MODE_LOHI) {
-            if (i < sym) below += c;
-            if (i == sym) s_csym = c;
-        }
     }
     const int amax = block_argmax(bp, bi, red);
-    const int total = block_sum_i(cs, red);
-    const int deficit = T - total;
-
-    if (MODE == MODE_LOHI) {
-        const int below_all = block_sum_i(below, red);
-        if (tid == 0) {
-            const uint32_t lo = (uint32_t)(below_all + (amax < sym ? deficit : 0));
-            const uint32_t hi = lo + (uint32_t)(s_csym + (amax == sym ? deficit : 0));
-            reinterpret_cast<uint2*>(out)[row] = make_uint2(lo, hi);
+    const int deficit = T - block_sum_i(cs, red);
+    s_wsum[tid] = cs + ((amax >= a && amax < e) ? deficit : 0);
+    __syncthreads();
+    if (tid == 0) {  // exclusive prefix over threads (integers, exact)
+        int run = 0;
+        for (int t = 0; t < CDF_NT; ++t) {
+            const int v = s_wsum[t];
+            s_wsum[t] = run;
+            run += v;
         }
-        return;
-    }
-
-    // ---- per-segment prefix (deficit folded into the argmax segment) --------
-    const int segd = cs + ((amax >= a && amax < e) ? deficit : 0);
-    const int excl = block_excl_scan_i(segd, red);
-
-    if (MODE == MODE_COUNTS || MODE == MODE_CDF) {
-        int32_t* o = reinterpret_cast<int32_t*>(out) + (int64_t)row * (V + 1);
-        if (tid == 0) o[0] = 0;
-        int run = excl;
-        for (int i = a; i < e; ++i) {
-            const int c = count(prob(i)) + (i == amax ? deficit : 0);
-            run += c;
-            o[i + 1] = (MODE == MODE_COUNTS) ? c : run;
-        }
-        return;
-    }
-
-    // ---- DECODE: locate target, then narrow the range ----------------------
-    const uint32_t target = s_target;
-    if (segd > 0 && (uint32_t)excl <= target && target < (uint32_t)(excl + segd)) {
-        s_owner = tid;
-        s_owner_base = excl;
     }
     __syncthreads();
-    if (tid < 32) {
-        const int lane = tid;
-        const int oa = min(s_owner * L, V), oe = min(oa + L, V);
-        const int q = (oe - oa + 31) / 32;
-        const int la = min(oa + lane * q, oe), le = min(la + q, oe);
-        int ls = 0;
-        for (int i = la; i < le; ++i) ls += count(prob(i)) + (i == amax ? deficit : 0);
+    int run = s_wsum[tid];
+    int32_t* o = out + (int64_t)row * (V + 1);
+    if (tid == 0) o[0] = 0;
+    for (int i = a; i < e; ++i) {
+        run += (int)floorf(__fmul_rn(__fdiv_rn(x[i], S), scale)) + 1 + (i == amax ? deficit : 0);
+        o[i + 1] = run;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// logits -> CDF / (lo, hi) / decode step
+// ---------------------------------------------------------------------------
+struct RowShared {
+    float2 wpart[CDF_NW];
+    float M, inv;
+    int amax;
+    int csym;
+};
+
+// Normaliser (M, 1/S), per-subtile factors gs[u] and the argmax of one row.
+// part(u) -> float2 (m_u, s_u); is_one(i) -> true iff e_i == 1.0.
+template <class Part, class IsOne>
+__device__ __forceinline__ void row_setup(Part part, IsOne is_one, int nsub, float scale,
+                                          float* gs, RowShared& rs, CdfRed& red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    MS acc{-INFINITY, 0.0f};
+    for (int u = tid; u < nsub; u += CDF_NT) {
+        const float2 p = part(u);
+        acc = ms_merge(acc, MS{p.x, p.y});
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = ms_merge(acc, ms_shfl_xor(acc, off));
+    if (lane == 0) rs.wpart[warp] = make_float2(acc.m, acc.s);
+    __syncthreads();
+    if (warp == 0) {
+        MS w{-INFINITY, 0.0f};
+        if (lane < CDF_NW) w = MS{rs.wpart[lane].x, rs.wpart[lane].y};
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) w = ms_merge(w, ms_shfl_xor(w, off));
+        if (lane == 0) {
+            rs.M = w.m;
+            rs.inv = __frcp_rn(w.s);
+        }
+    }
+    __syncthreads();
+    const float M = rs.M, inv = rs.inv;
+    float best = -INFINITY;
+    int bu = INT_MAX;
+    for (int u = tid; u < nsub; u += CDF_NT) {
+        const float g = __fmul_rn(__fmul_rn(kb_expf(__fsub_rn(part(u).x, M)), inv), scale);
+        gs[u] = g;
+        if (g > best) {
+            best = g;
+            bu = u;
+        }
+    }
+    const int ustar = block_argmax(best, bu, red);  // contains __syncthreads
+    if (warp == 0) {
+        const int a = ustar * SUBTILE;
+        const unsigned b0 = __ballot_sync(0xffffffffu, is_one(a + lane));
+        const unsigned b1 = __ballot_sync(0xffffffffu, is_one(a + 32 + lane));
+        if (lane == 0) rs.amax = b0 ? a + __ffs(b0) - 1 : a + 32 + __ffs(b1) - 1;
+    }
+    __syncthreads();
+}
+
+// Counts of the 8 consecutive elements i0..i0+7 (< lim).
+__device__ __forceinline__ int counts8(const float (&e)[8], float g, int i0, int lim, int (&c)[8]) {
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        c[k] = (i0 + k < lim) ? (int)floorf(__fmul_rn(e[k], g)) + 1 : 0;
+        sum += c[k];
+    }
+    return sum;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& q, float (&e)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h[k]);
+        e[2 * k] = f.x;
+        e[2 * k + 1] = f.y;
+    }
+}
+
+// Element source: numerators stored (global or shared), 16-byte loads.
+struct NumSrc {
+    const uint16_t* x;
+    int V;
+    __device__ __forceinline__ void load8(int i0, int lim, float (&e)[8]) const {
+        if (((reinterpret_cast<uintptr_t>(x + i0)) & 15u) == 0 && i0 + 8 <= lim) {
+            unpack8(*reinterpret_cast<const uint4*>(x + i0), e);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) e[k] = (i0 + k < lim) ? h2f(x[i0 + k]) : 0.0f;
+        }
+    }
+    __device__ __forceinline__ bool is_one(int i) const {
+        return i < V && x[i] == (uint16_t)0x3C00u;
+    }
+};
+
+// Element source: raw logits; numerators computed against the subtile max.
+struct RawSrc {
+    const uint16_t* x;
+    const float2* part;
+    int V;
+    __device__ __forceinline__ void load8(int i0, int lim, float (&e)[8]) const {
+        const float m = part[i0 / SUBTILE].x;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            e[k] = (i0 + k < lim) ? h2f(exp_rel_f16(h2f(x[i0 + k]), m)) : 0.0f;
+    }
+    __device__ __forceinline__ bool is_one(int i) const {
+        return i < V && exp_rel_f16(h2f(x[i]), part[i / SUBTILE].x) == (uint16_t)0x3C00u;
+    }
+};
+
+// Subtile partials of a raw logits row into smem (softmax_stats.cuh spec).
+__device__ __forceinline__ void raw_partials(const uint16_t* x, int V, int nsub, float2* out) {
+    for (int u = threadIdx.x; u < nsub; u += CDF_NT) {
+        const int a = u * SUBTILE, e = min(a + SUBTILE, V);
+        float m = -INFINITY;
+        for (int i = a; i < e; ++i) m = fmaxf(m, h2f(x[i]));
+        float sum = 0.0f;
+        for (int i = a; i < e; ++i) sum = __fadd_rn(sum, h2f(exp_rel_f16(h2f(x[i]), m)));
+        out[u] = make_float2(m, sum);
+    }
+    __syncthreads();
+}
+
+// Walk the warp's range in 256-element steps: per step each lane's 8 counts
+// (deficit added at the argmax) and their warp-inclusive prefix.  f(i0, c,
+// ls, excl_in_warp_step, step_total) is called for every step; returning
+// true stops the walk.
+template <class Src, class F>
+__device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int wa, int we,
+                                            int amax, int deficit, F f) {
+    const int lane = threadIdx.x & 31;
+    for (int base = wa; base < we; base += 256) {
+        const int i0 = base + lane * 8;
+        int c[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ls = 0;
+        if (i0 < we) {
+            float e[8];
+            src.load8(i0, we, e);
+            ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (i0 + k == amax) c[k] += deficit;
+            if (amax >= i0 && amax < i0 + 8) ls += deficit;
+        }
         int inc = ls;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
             const int y = __shfl_up_sync(0xffffffffu, inc, off);
             if (lane >= off) inc += y;
         }
-        const int base = s_owner_base + inc - ls;
-        if (ls > 0 && (uint32_t)base <= target && target < (uint32_t)(base + ls)) {
-            int run = base;
-            for (int i = la; i < le; ++i) {
-                const int c = count(prob(i)) + (i == amax ? deficit : 0);
-                if (target < (uint32_t)(run + c)) {
-                    s_sym = i;
-                    s_lo = (uint32_t)run;
-                    s_hi = (uint32_t)(run + c);
-                    break;
+        const int total = __shfl_sync(0xffffffffu, inc, 31);
+        if (f(i0, c, ls, inc - ls, total)) break;
+    }
+}
+
+template <int MODE, class Src>
+__device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, RowShared& rs,
+                             CdfRed& red, int row, int sym, void* out, const uint8_t* in,
+                             int64_t in_bytes, const int64_t* in_offs, uint32_t* states,
+                             int32_t* counters, int32_t* out_syms, int32_t* history,
+                             int64_t hist_stride) {
+    __shared__ int s_wsum[CDF_NW], s_wexcl[CDF_NW], s_owner, s_sym;
+    __shared__ uint32_t s_target, s_lo, s_hi;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int T = 1 << bits;
+    const int Lw = ((V + CDF_NW * 256 - 1) / (CDF_NW * 256)) * 256;
+    const int wa = min(warp * Lw, V), we = min(wa + Lw, V);
+    const int amax = rs.amax;
+    if (MODE == MODE_DECODE && tid == 0) s_target = decode_target(states + 4 * (int64_t)row, bits);
+
+    // ---- element pass: totals (and the prefix below the symbol) ----------
+    int cs = 0, below = 0;
+    for (int base = wa; base < we; base += 256) {
+        const int i0 = base + lane * 8;
+        if (i0 >= we) continue;
+        float e[8];
+        int c[8];
+        src.load8(i0, we, e);
+        const int step = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+        cs += step;
+        if (MODE == MODE_LOHI) {
+            if (i0 + 8 <= sym) {
+                below += step;
+            } else if (i0 <= sym) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (i0 + k < sym) below += c[k];
+                    if (i0 + k == sym) rs.csym = c[k];
                 }
-                run += c;
             }
         }
+    }
+    const int deficit = T - block_sum_i(cs, red);
+    if (MODE == MODE_LOHI) {
+        const int below_all = block_sum_i(below, red);
+        if (tid == 0) {
+            const uint32_t lo = (uint32_t)(below_all + (amax < sym ? deficit : 0));
+            const uint32_t hi = lo + (uint32_t)(rs.csym + (amax == sym ? deficit : 0));
+            reinterpret_cast<uint2*>(out)[row] = make_uint2(lo, hi);
+        }
+        return;
+    }
+
+    // ---- per-warp totals (deficit on the argmax's warp), exclusive scan ----
+    int ws = cs;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, off);
+    if (lane == 0) s_wsum[warp] = ws + ((amax >= wa && amax < we) ? deficit : 0);
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int w = 0; w < CDF_NW; ++w) {
+            s_wexcl[w] = run;
+            run += s_wsum[w];
+        }
+    }
+    __syncthreads();
+
+    if (MODE == MODE_COUNTS || MODE == MODE_CDF) {
+        int32_t* o = reinterpret_cast<int32_t*>(out) + (int64_t)row * (V + 1);
+        if (tid == 0) o[0] = 0;
+        int run = s_wexcl[warp];
+        walk_counts(src, gs, wa, we, amax, deficit,
+                    [&](int i0, const int (&c)[8], int, int excl, int total) {
+                        if (i0 < we) {
+                            int r = run + excl;
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                if (i0 + k < we) {
+                                    r += c[k];
+                                    o[i0 + k + 1] = (MODE == MODE_COUNTS) ? c[k] : r;
+                                }
+                            }
+                        }
+                        run += total;
+                        return false;
+                    });
+        return;
+    }
+
+    // ---- DECODE: owner warp, then the step and lane holding the target -----
+    const uint32_t target = s_target;
+    if (tid < CDF_NW && s_wsum[tid] > 0 && (uint32_t)s_wexcl[tid] <= target &&
+        target < (uint32_t)(s_wexcl[tid] + s_wsum[tid]))
+        s_owner = tid;
+    __syncthreads();
+    if (warp == s_owner) {
+        int run = s_wexcl[warp];
+        walk_counts(src, gs, wa, we, amax, deficit,
+                    [&](int i0, const int (&c)[8], int ls, int excl, int total) {
+                        if (target >= (uint32_t)(run + total)) {
+                            run += total;
+                            return false;
+                        }
+                        int r = run + excl;
+                        if (ls > 0 && (uint32_t)r <= target && target < (uint32_t)(r + ls)) {
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                if (c[k] > 0 && target < (uint32_t)(r + c[k])) {
+                                    s_sym = i0 + k;
+                                    s_lo = (uint32_t)r;
+                                    s_hi = (uint32_t)(r + c[k]);
+                                    break;
+                                }
+                                r += c[k];
+                            }
+                        }
+                        return true;
+                    });
     }
     __syncthreads();
     if (tid == 0) {
@@ -337,28 +452,78 @@ __global__ void __launch_bounds__(CDF_NT) k_cdf(const void* __restrict__ src, in
     }
 }
 
-template <int MODE, bool FROM_PROBS>
-static int launch_cdf(int rows, int V, const void* src, int64_t stride, int bits,
-                      const int32_t* symbols, void* out, const uint8_t* in, int64_t in_bytes,
-                      const int64_t* in_offs, uint32_t* states, int32_t* counters,
-                      int32_t* out_syms, int32_t* history, int64_t hist_stride, cudaStream_t st) {
-    const size_t smem = FROM_PROBS ? 0 : (size_t)((V * 2 + 15) / 16) * 16;
-    static int configured = 0;  // per template instance
-    if (!FROM_PROBS && smem > 48 * 1024 && !configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_cdf<MODE, FROM_PROBS>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(66 * 1024 * 2));
-        if (e != cudaSuccess) {
-            set_cuda_error(e);
-            return KB_ERR_CUDA;
-        }
-        configured = 1;
+// One CTA per row; numerators + partials from global (stats != NULL) or raw
+// logits (stats == NULL).
+template <int MODE>
+__global__ void __launch_bounds__(CDF_NT) k_cdf(const uint16_t* __restrict__ logits, int64_t stride,
+                                                int V, int bits, const float2* __restrict__ stats,
+                                                int64_t stats_stride,
+                                                const int32_t* __restrict__ symbols, void* out,
+                                                const uint8_t* in, int64_t in_bytes,
+                                                const int64_t* __restrict__ in_offs,
+                                                uint32_t* states, int32_t* counters,
+                                                int32_t* out_syms, int32_t* history,
+                                                int64_t hist_stride) {
+    __shared__ float2 s_part[MAX_SUB];
+    __shared__ float s_gs[MAX_SUB];
+    __shared__ RowShared rs;
+    __shared__ CdfRed red;
+    const int row = blockIdx.x;
+    if (MODE == MODE_DECODE && counters && counters[2 * row] >= counters[2 * row + 1]) {
+        if (threadIdx.x == 0) out_syms[row] = 0;
+        return;
     }
+    const uint16_t* x = logits + (int64_t)row * stride;
+    const int nsub = (V + SUBTILE - 1) / SUBTILE;
+    const float scale = (float)((1 << bits) - V);
+    int sym = 0;
+    if (MODE == MODE_LOHI) {
+        sym = symbols[row];
+        sym = sym < 0 ? 0 : (sym >= V ? V - 1 : sym);
+    }
+    if (stats) {
+        const float2* p = stats + (int64_t)row * stats_stride;
+        const NumSrc src{x, V};
+        row_setup([&](int u) { return p[u]; }, [&](int i) { return src.is_one(i); }, nsub, scale,
+                  s_gs, rs, red);
+        cdf_row_body<MODE>(src, V, bits, s_gs, rs, red, row, sym, out, in, in_bytes, in_offs,
+                           states, counters, out_syms, history, hist_stride);
+    } else {
+        raw_partials(x, V, nsub, s_part);
+        const RawSrc src{x, s_part, V};
+        row_setup([&](int u) { return s_part[u]; }, [&](int i) { return src.is_one(i); }, nsub,
+                  scale, s_gs, rs, red);
+        cdf_row_body<MODE>(src, V, bits, s_gs, rs, red, row, sym, out, in, in_bytes, in_offs,
+                           states, counters, out_syms, history, hist_stride);
+    }
+}
+
+struct CdfArgs {
+    const uint16_t* logits;
+    int64_t stride;
+    int V, bits;
+    const float* stats;
+    int64_t stats_stride;
+    const int32_t* symbols;
+    void* out;
+    const uint8_t* in;
+    int64_t in_bytes;
+    const int64_t* in_offs;
+    uint32_t* states;
+    int32_t* counters;
+    int32_t* out_syms;
+    int32_t* history;
+    int64_t hist_stride;
+};
+
+template <int MODE>
+static int launch_cdf(int rows, const CdfArgs& a, cudaStream_t st) {
     ProfScope ps(MODE == MODE_DECODE ? PH_DECODE : PH_CDF, st,
-                 (double)rows * ((double)V * (FROM_PROBS ? 4 : 2) + 16.0));
-    k_cdf<MODE, FROM_PROBS><<<rows, CDF_NT, smem, st>>>(src, stride, V, bits, symbols, out, in,
-                                                         in_bytes, in_offs, states, counters,
-                                                         out_syms, history, hist_stride);
+                 (double)rows * ((double)a.V * 2 + 16.0));
+    k_cdf<MODE><<<rows, CDF_NT, 0, st>>>(a.logits, a.stride, a.V, a.bits,
+                                         reinterpret_cast<const float2*>(a.stats), a.stats_stride,
+                                         a.symbols, a.out, a.in, a.in_bytes, a.in_offs, a.states,
+                                         a.counters, a.out_syms, a.history, a.hist_stride);
     return launch_status();
 }
 
@@ -367,29 +532,34 @@ static int launch_cdf(int rows, int V, const void* src, int64_t stride, int bits
 using namespace kb;
 
 static inline bool cdf_args_ok(int V, int bits) {
-    // V < T so that T - V >= 1; V <= 65536 bounds the shared-memory row copy.
+    // V < T so that T - V >= 1; V <= 65536 bounds the subtile partials per row.
     return bits >= 2 && bits <= 30 && V >= 1 && V <= 65536 && V < (1 << bits);
 }
 
+static inline bool stats_ok(const float* stats, int64_t stats_stride, int V) {
+    // stats_stride >= number of 64-column subtiles, float2-aligned
+    return !stats || (stats_stride >= (V + SUBTILE - 1) / SUBTILE &&
+                      (reinterpret_cast<uintptr_t>(stats) & 7u) == 0);
+}
+
 extern "C" int kb_cdf_rows(const uint16_t* logits, int64_t row_stride, int rows, int V, int bits,
-                           int mode, const int32_t* symbols, void* out, void* stream) {
-    if (!logits || !out || rows < 0 || !cdf_args_ok(V, bits) || row_stride < V) return KB_ERR_ARG;
+                           int mode, const float* logit_stats, int64_t stats_stride,
+                           const int32_t* symbols, void* out, void* stream) {
+    if (!logits || !out || rows < 0 || !cdf_args_ok(V, bits) || row_stride < V ||
+        !stats_ok(logit_stats, stats_stride, V))
+        return KB_ERR_ARG;
     if (rows == 0) return KB_OK;
     cudaStream_t st = as_stream(stream);
+    CdfArgs a{logits, row_stride, V, bits, logit_stats, stats_stride, symbols, out,
+              nullptr, 0, nullptr, nullptr, nullptr, nullptr, nullptr, 0};
     switch (mode) {
-        case KB_CDF_COUNTS:
-            return launch_cdf<MODE_COUNTS, false>(rows, V, logits, row_stride, bits, nullptr, out,
-                                                  nullptr, 0, nullptr, nullptr, nullptr, nullptr,
-                                                  nullptr, 0, st);
-        case KB_CDF_CDF:
-            return launch_cdf<MODE_CDF, false>(rows, V, logits, row_stride, bits, nullptr, out,
-                                               nullptr, 0, nullptr, nullptr, nullptr, nullptr, nullptr, 0, st);
-        case KB_CDF_LOHI:
+        case KB_CDF_COUNTS: return launch_cdf<MODE_COUNTS>(rows, a, st);
+        case KB_CDF_CDF: return launch_cdf<MODE_CDF>(rows, a, st);
+        case KB_CDF_LOHI: {
             if (!symbols) return KB_ERR_ARG;
             if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return KB_ERR_ALIGN;
-            return launch_cdf<MODE_LOHI, false>(rows, V, logits, row_stride, bits, symbols, out,
-                                                nullptr, 0, nullptr, nullptr, nullptr, nullptr,
-                                                nullptr, 0, st);
+            return launch_cdf<MODE_LOHI>(rows, a, st);
+        }
         default:
             return KB_ERR_ARG;
     }
@@ -399,21 +569,23 @@ extern "C" int kb_cdf_from_probs(const float* probs, int rows, int V, int bits, 
                                  void* stream) {
     if (!probs || !out || rows < 0 || !cdf_args_ok(V, bits)) return KB_ERR_ARG;
     if (rows == 0) return KB_OK;
-    return launch_cdf<MODE_CDF, true>(rows, V, probs, V, bits, nullptr, out, nullptr, 0, nullptr,
-                                      nullptr, nullptr, nullptr, nullptr, 0, as_stream(stream));
+    cudaStream_t st = as_stream(stream);
+    ProfScope ps(PH_CDF, st, (double)rows * ((double)V * 4 + 16.0));
+    k_cdf_probs<<<rows, CDF_NT, 0, st>>>(probs, V, bits, out);
+    return launch_status();
 }
 
 extern "C" int kb_decode_logits_step(const uint16_t* logits, int64_t row_stride, int B, int V,
-                                     int bits, const uint8_t* in, int64_t in_bytes,
-                                     const int64_t* in_offs, uint32_t* states, int32_t* counters,
-                                     int32_t* out_syms, int32_t* history, int64_t hist_stride,
-                                     void* stream) {
+                                     int bits, const float* logit_stats, int64_t stats_stride,
+                                     const uint8_t* in, int64_t in_bytes, const int64_t* in_offs,
+                                     uint32_t* states, int32_t* counters, int32_t* out_syms,
+                                     int32_t* history, int64_t hist_stride, void* stream) {
     if (!logits || !in || !states || !out_syms || B < 0 || !cdf_args_ok(V, bits) ||
-        row_stride < V || hist_stride < 0)
+        row_stride < V || hist_stride < 0 || !stats_ok(logit_stats, stats_stride, V))
         return KB_ERR_ARG;
     if (B > 1 && !in_offs) return KB_ERR_ARG;
     if (B == 0) return KB_OK;
-    return launch_cdf<MODE_DECODE, false>(B, V, logits, row_stride, bits, nullptr, nullptr, in,
-                                          in_bytes, in_offs, states, counters, out_syms, history,
-                                          hist_stride, as_stream(stream));
+    CdfArgs a{logits, row_stride, V, bits, logit_stats, stats_stride, nullptr, nullptr,
+              in, in_bytes, in_offs, states, counters, out_syms, history, hist_stride};
+    return launch_cdf<MODE_DECODE>(B, a, as_stream(stream));
 }

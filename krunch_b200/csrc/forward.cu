@@ -189,11 +189,11 @@ extern "C" size_t kb_forward_workspace_bytes(const kb_model* m, int B, int T) {
 
 extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B, int T,
                                  float* state, void* ws, size_t ws_bytes, uint16_t* logits,
-                                 void* stream) {
+                                 float* logit_stats, void* stream) {
     if (!m || !tokens || !state || !ws || !logits || B <= 0 || T <= 0) return KB_ERR_ARG;
     const kb_model_desc& d = m->d;
     if (ws_bytes < layout(d, B, T, nullptr, nullptr)) return KB_ERR_WORKSPACE;
-    if (!aligned16(ws) || !aligned16(logits)) return KB_ERR_ALIGN;
+    if (!aligned16(ws) || !aligned16(logits) || ((uintptr_t)logit_stats & 7u)) return KB_ERR_ALIGN;
     cudaStream_t st = as_stream(stream);
     Workspace w;
     layout(d, B, T, reinterpret_cast<char*>(ws), &w);
@@ -254,8 +254,13 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
     }
     {
         ProfScope ps(PH_HEAD, st, 2.0 * R * (double)d.n_vocab * C);
-        KB_TRY(launch_gemm_f16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C, KB_EPI_F16,
-                               logits, d.vocab_pad, nullptr, nullptr, st));
+        if (logit_stats)
+            KB_TRY(launch_gemm_logits(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
+                                      logits, d.vocab_pad, d.n_vocab, logit_stats,
+                                      d.vocab_pad / 64, st));
+        else
+            KB_TRY(launch_gemm_f16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
+                                   KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));
     }
     return KB_OK;
 }
@@ -303,5 +308,6 @@ extern "C" int kb_forward_window_noalloc(const kb_model* m, const int32_t* token
     void* ws = nullptr;
     const int rc = noalloc_scratch(&ws);
     if (rc != KB_OK) return rc;
-    return kb_forward_window(m, tokens, B, T, state, ws, KB_NOALLOC_SCRATCH_BYTES, logits, stream);
+    return kb_forward_window(m, tokens, B, T, state, ws, KB_NOALLOC_SCRATCH_BYTES, logits, nullptr,
+                             stream);
 }

@@ -6,9 +6,13 @@
 //               into a 4-stage shared-memory ring, no cluster multicast;
 //   warp 1      MMA issuer: 4 x tcgen05.mma 128x256x16 per stage into one of
 //               two TMEM accumulators (2 x 256 fp32 columns);
-//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes, the fused
-//               epilogue, 16-byte stores; draining accumulator i overlaps
-//               the MMAs of tile i+1.
+//   warps 2..17 epilogue: each warp owns 32 TMEM lanes (warp % 4) and one
+//               64-column quarter of the tile; tcgen05.ld, the fused epilogue,
+//               16-byte stores.  Draining accumulator i overlaps the MMAs of
+//               tile i+1.  The head's epilogue stores, instead of the logits,
+//               e^(x - m_u) in fp16 for every 64-column subtile u together
+//               with the subtile's (m_u, sum), so the CDF kernel needs no exp
+//               per element (softmax_stats.cuh).
 // Output tile (m, n) walks K from 0 to K in 64-wide blocks, 16 per MMA, for
 // every M: a row's result does not depend on M or on the other rows (the
 // M-invariance the decoder relies on, krunch_ac/cuda/det_matmul_tc*.cu).
@@ -19,11 +23,13 @@
 #include <mutex>
 
 #include "rwkv_ops.cuh"
+#include "softmax_stats.cuh"
 #include "tc_common.cuh"
 
 namespace kb {
 
-constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4, TC_NT = 192;
+constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4, TC_NT = 576;
+constexpr int TC_EPI_WARPS = 16;
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;          // 16 KB
 constexpr uint32_t TC_B_BYTES = TC_BN * TC_BK * 2;          // 32 KB
 constexpr uint32_t TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;  // 48 KB
@@ -116,7 +122,7 @@ template <int EPI>
 __global__ void __launch_bounds__(TC_NT, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               int M, int N, int K, void* out, int64_t ldo, const uint16_t* resid,
-              const uint16_t* gate) {
+              const uint16_t* gate, int V, float2* stats, int stats_stride) {
     extern __shared__ unsigned char tc_smem_raw[];
     const uint32_t raw = tc::smem_addr(tc_smem_raw);
     unsigned char* smem = tc_smem_raw + (((raw + 1023u) & ~1023u) - raw);
@@ -134,7 +140,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
         }
         for (int a = 0; a < 2; ++a) {
             tc::mbar_init(&bars->tfull[a], 1);
-            tc::mbar_init(&bars->tempty[a], 4);
+            tc::mbar_init(&bars->tempty[a], TC_EPI_WARPS);
         }
         bars->abort = 0;
         tc::fence_barrier_init();
@@ -219,8 +225,9 @@ __global__ void __launch_bounds__(TC_NT, 1)
             }
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
-        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        // ---------------- epilogue (warps 2..17) ----------------
+        const int q = warp & 3;          // TMEM lane quadrant this warp may access
+        const int g = (warp - 2) >> 2;   // 64-column quarter of the tile
         int i = 0;
         for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
             const int a = i & 1;
@@ -233,14 +240,64 @@ __global__ void __launch_bounds__(TC_NT, 1)
             tc::fence_after_sync();
             const int64_t row = m0 + q * 32 + lane;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * TC_BN);
+            if (EPI == KB_EPI_LOGITS_STATS) {
+                // pass 1: subtile max of the fp16-rounded logits (columns < V)
+                float m = -INFINITY;
 #pragma unroll 1
-            for (int c = 0; c < TC_BN / 32; ++c) {
-                const int col0 = n0 + c * 32;
-                if (col0 >= N) break;
-                uint32_t v[32];
-                tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
-                tc::tmem_ld_wait();
-                if (row < M) tc_epi_store<EPI>(v, out, ldo, resid, gate, row, col0);
+                for (int c = 2 * g; c < 2 * g + 2; ++c) {
+                    const int col0 = n0 + c * 32;
+                    if (col0 >= N) break;
+                    uint32_t v[32];
+                    tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (col0 + j < V) m = fmaxf(m, __half2float(__float2half_rn(u2f(v[j]))));
+                }
+                // pass 2: e = fp16(e^(x - m)), left-to-right sum, store e
+                float s = 0.0f;
+#pragma unroll 1
+                for (int c = 2 * g; c < 2 * g + 2; ++c) {
+                    const int col0 = n0 + c * 32;
+                    if (col0 >= N) break;
+                    uint32_t v[32];
+                    tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    tc::tmem_ld_wait();
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        uint16_t e0 = 0, e1 = 0;
+                        if (col0 + j < V) {
+                            e0 = exp_rel_f16(__half2float(__float2half_rn(u2f(v[j]))), m);
+                            s = __fadd_rn(s, h2f(e0));
+                        }
+                        if (col0 + j + 1 < V) {
+                            e1 = exp_rel_f16(__half2float(__float2half_rn(u2f(v[j + 1]))), m);
+                            s = __fadd_rn(s, h2f(e1));
+                        }
+                        packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
+                    }
+                    if (row < M) {
+                        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) +
+                                                              row * ldo + col0);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                                                packed[4 * j + 3]);
+                    }
+                }
+                const int u = (n0 + 64 * g) / SUBTILE;
+                if (row < M && u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
+            } else {
+#pragma unroll 1
+                for (int c = 2 * g; c < 2 * g + 2; ++c) {
+                    const int col0 = n0 + c * 32;
+                    if (col0 >= N) break;
+                    uint32_t v[32];
+                    tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
+                    tc::tmem_ld_wait();
+                    if (row < M) tc_epi_store<EPI>(v, out, ldo, resid, gate, row, col0);
+                }
             }
             tc::fence_before_sync();
             __syncwarp();
@@ -304,7 +361,7 @@ int sm_count() {
 template <int EPI>
 int launch_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N, int K,
               void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
-              cudaStream_t st) {
+              cudaStream_t st, int V = 0, float2* stats = nullptr, int stats_stride = 0) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
@@ -320,7 +377,8 @@ int launch_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, in
         return KB_ERR_UNSUPPORTED;
     const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    k_gemm_tc<EPI><<<grid, TC_NT, TC_SMEM, st>>>(ma, mb, M, N, K, out, ldo, resid, gate);
+    k_gemm_tc<EPI><<<grid, TC_NT, TC_SMEM, st>>>(ma, mb, M, N, K, out, ldo, resid, gate, V, stats,
+                                                  stats_stride);
     return launch_status();
 }
 
@@ -339,6 +397,14 @@ int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ld
         case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
         default: return KB_ERR_ARG;
     }
+}
+
+int launch_gemm_logits(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M,
+                       int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
+                       int stats_stride, cudaStream_t st) {
+    if (M == 0) return KB_OK;
+    return launch_tc<KB_EPI_LOGITS_STATS>(A, lda, W, ldw, M, N, K, out, ldo, nullptr, nullptr, st,
+                                          V, reinterpret_cast<float2*>(stats), stats_stride);
 }
 
 int read_tc_error(int reset) {

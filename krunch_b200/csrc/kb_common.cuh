@@ -40,12 +40,12 @@ constexpr uint32_t RC_THREE_QTR = RC_HALF + RC_QTR;
 // (no contraction, no approximate hardware units) so that a plain C
 // restatement reproduces it bit for bit.
 //
-// Method: Cody-Waite range reduction x = n*ln2 + r with ln2 split into a
-// 12-bit head (exact n*head for |n| < 2^12) and a tail; e^r by its degree-6
-// Taylor polynomial in Horner form (|r| <= 0.35, truncation < 1.5e-7
-// relative); scaling by 2^n through the exponent field.  Inputs below -86
-// return 0 (keeps every result a normal number, so flush-to-zero settings
-// cannot change bits); NaN returns 0.  Inputs must be <= 88.
+// Method: e^x = 2^y with y = x * log2(e) (one rounding); y = n + f with
+// n = rint(y), |f| <= 1/2; 2^f by the degree-5 Taylor polynomial of
+// e^(f ln 2) in Horner form (truncation < 2.6e-6 relative); 2^n added to the
+// exponent field.  Relative error below 7e-6 over the domain.  Inputs below
+// -86 return 0 (so every result is a normal number and flush-to-zero
+// settings cannot change bits); NaN returns 0.  Inputs must be <= 88.
 // ---------------------------------------------------------------------------
 __host__ __device__ inline float kb_bits_to_float(uint32_t u) {
 #ifdef __CUDA_ARCH__
@@ -59,21 +59,17 @@ __host__ __device__ inline float kb_bits_to_float(uint32_t u) {
 
 __device__ __forceinline__ float kb_expf(float x) {
     if (!(x >= -86.0f)) return 0.0f;
-    const float LOG2E = kb_bits_to_float(0x3fb8aa3bu);   // 1/ln2 rounded to fp32
-    const float LN2_HI = kb_bits_to_float(0x3f317000u);  // ln2 with 12 low bits cleared
-    const float LN2_LO = kb_bits_to_float(0x3805fdf4u);  // ln2 - LN2_HI rounded
-    const float n = rintf(__fmul_rn(x, LOG2E));
-    float r = __fmaf_rn(-n, LN2_HI, x);
-    r = __fmaf_rn(-n, LN2_LO, r);
-    float p = 1.0f / 720.0f;
-    p = __fmaf_rn(p, r, 1.0f / 120.0f);
-    p = __fmaf_rn(p, r, 1.0f / 24.0f);
-    p = __fmaf_rn(p, r, 1.0f / 6.0f);
-    p = __fmaf_rn(p, r, 0.5f);
-    p = __fmaf_rn(p, r, 1.0f);
-    p = __fmaf_rn(p, r, 1.0f);
-    const uint32_t e = (uint32_t)((int)n + 127) << 23;
-    return __fmul_rn(p, __uint_as_float(e));
+    const float LOG2E = kb_bits_to_float(0x3fb8aa3bu);  // 1/ln2 rounded to fp32
+    const float y = __fmul_rn(x, LOG2E);
+    const float n = rintf(y);
+    const float f = __fsub_rn(y, n);
+    float p = kb_bits_to_float(0x3aaec3ffu);             // ln2^5/5!
+    p = __fmaf_rn(p, f, kb_bits_to_float(0x3c1d955bu));  // ln2^4/4!
+    p = __fmaf_rn(p, f, kb_bits_to_float(0x3d635847u));  // ln2^3/3!
+    p = __fmaf_rn(p, f, kb_bits_to_float(0x3e75fdf0u));  // ln2^2/2!
+    p = __fmaf_rn(p, f, kb_bits_to_float(0x3f317218u));  // ln2
+    p = __fmaf_rn(p, f, 1.0f);
+    return __int_as_float(__float_as_int(p) + (int)n * (1 << 23));
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) {

@@ -30,6 +30,13 @@ int launch_gemm_f16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t l
 int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
                    int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
                    const uint16_t* gate, cudaStream_t st);
+// Head GEMM: per row and 64-column subtile u, out holds fp16 e^(x - m_u) of
+// the fp16-rounded logits x (0 past column V) and stats[row * stats_stride + u]
+// = (m_u, sum of those e), as defined in softmax_stats.cuh.
+constexpr int KB_EPI_LOGITS_STATS = 6;
+int launch_gemm_logits(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M,
+                       int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
+                       int stats_stride, cudaStream_t st);
 // Device-side error code of the tcgen05 kernels (0 = none); optionally reset.
 int read_tc_error(int reset);
 

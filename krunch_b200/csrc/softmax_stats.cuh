@@ -1,0 +1,44 @@
+// Softmax pieces shared by the head GEMM epilogue (gemm_tc.cu) and the CDF
+// kernels (cdf.cu).
+//
+// A logits row x (fp16 values) is cut into 64-column subtiles.  For subtile u
+// with columns [64u, min(64u+64, V)):
+//   m_u  = max x_i
+//   e_i  = fp16(kb_expf(x_i - m_u))                  (stored by the head GEMM)
+//   s_u  = sum_i e_i, left to right in fp32
+// The row normaliser (M, S) merges the (m_u, s_u): thread t of 512 merges
+// u = t, t+512, ... in order, each warp combines in a xor butterfly, then the
+// 16 warp results (padded to 32 with the neutral (-inf, 0)) combine in the
+// same butterfly.  merge() keeps the larger max and adds the other sum scaled
+// by e^(m_small - m_large) (ties add the sums); it is symmetric, so every
+// lane ends with the same bits.  Then, with scale = T - V,
+//   gs_u = (kb_expf(m_u - M) * (1/S)) * scale,   q_i = e_i * gs_u,
+//   c_i  = floor(q_i) + 1,   argmax = smallest i with the largest q_i.
+// All arithmetic is explicitly rounded and exp is kb_expf, so a plain C
+// restatement reproduces every value bit for bit.
+#pragma once
+#include "kb_common.cuh"
+
+namespace kb {
+
+constexpr int SUBTILE = 64;  // columns per softmax partial
+
+struct MS {
+    float m, s;
+};
+
+__device__ __forceinline__ MS ms_merge(MS a, MS b) {
+    if (a.m >= b.m) return MS{a.m, __fadd_rn(a.s, __fmul_rn(b.s, kb_expf(__fsub_rn(b.m, a.m))))};
+    return MS{b.m, __fadd_rn(b.s, __fmul_rn(a.s, kb_expf(__fsub_rn(a.m, b.m))))};
+}
+
+__device__ __forceinline__ MS ms_shfl_xor(MS v, int off) {
+    return MS{__shfl_xor_sync(0xffffffffu, v.m, off), __shfl_xor_sync(0xffffffffu, v.s, off)};
+}
+
+// e_i of a logit relative to its subtile max, as stored (fp16 bits).
+__device__ __forceinline__ uint16_t exp_rel_f16(float x, float m) {
+    return f2h(kb_expf(__fsub_rn(x, m)));
+}
+
+}  // namespace kb

@@ -109,7 +109,7 @@ def det_softmax_cdf(logits: torch.Tensor, cdf_T: int) -> torch.Tensor:
     rows, V = logits.shape
     out = torch.empty((rows, V + 1), dtype=torch.int32, device=logits.device)
     N.call("kb_cdf_rows", logits.data_ptr(), V, rows, V, T.bit_length() - 1, N.KB_CDF_COUNTS,
-           None, out.data_ptr(), N.stream_ptr(logits.device))
+           None, 0, None, out.data_ptr(), N.stream_ptr(logits.device))
     return out
 
 

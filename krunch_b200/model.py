@@ -145,16 +145,27 @@ class RWKVModel:
     def new_logits(self, B: int, T: int) -> torch.Tensor:
         return torch.empty((B * T, self.spec.vocab_pad), dtype=torch.float16, device=self.device)
 
+    @property
+    def stats_stride(self) -> int:
+        """Softmax partials per logits row (one per 64 head columns)."""
+        return self.spec.vocab_pad // 64
+
+    def new_stats(self, B: int, T: int) -> torch.Tensor:
+        return torch.empty((B * T, self.stats_stride, 2), dtype=torch.float32, device=self.device)
+
     def forward_window(self, tokens: torch.Tensor, state: torch.Tensor, workspace: torch.Tensor,
-                       logits: torch.Tensor) -> torch.Tensor:
+                       logits: torch.Tensor, stats: torch.Tensor | None = None) -> torch.Tensor:
         """tokens int32 [B, T] (contiguous, on device) -> logits fp16 [B*T, vocab_pad].
 
-        ``state`` is read and advanced in place."""
+        ``state`` is read and advanced in place.  With ``stats`` (from
+        new_stats) the head writes, instead of raw logits, the per-64-column
+        softmax numerators into ``logits`` and their partials into ``stats``
+        (the input kb_cdf_rows / kb_decode_logits_step take)."""
         B, T = tokens.shape
         assert tokens.dtype == torch.int32 and tokens.is_contiguous()
         assert state.is_contiguous() and state.numel() == self.state_numel(B)
         assert logits.shape[0] >= B * T and logits.shape[1] == self.spec.vocab_pad
         N.call("kb_forward_window", self.handle, tokens.data_ptr(), B, T, state.data_ptr(),
                workspace.data_ptr(), workspace.numel(), logits.data_ptr(),
-               N.stream_ptr(self.device))
+               None if stats is None else stats.data_ptr(), N.stream_ptr(self.device))
         return logits

@@ -36,6 +36,9 @@ def lib():
         L.oc_dec_symbol.argtypes = [vp, vp, i32, i32]
         L.oc_decode_cdf.argtypes = [vp, i64, vp, i64, i64, i32, i32, vp]
         L.oc_dec_size.restype = i32
+        L.oc_softmax_parts.argtypes = [vp, i32, vp, vp]
+        L.oc_float_to_half.restype = C.c_uint16
+        L.oc_float_to_half.argtypes = [C.c_float]
         _lib = L
     return _lib
 
@@ -95,6 +98,26 @@ def lohi_from_logits(logits: np.ndarray, symbols: np.ndarray, bits: int,
     with cf.ThreadPoolExecutor(nt) as ex:
         list(ex.map(work, range(nt)))
     return out
+
+
+SUBTILE = 64
+
+
+def softmax_parts(logits: np.ndarray):
+    """Per 64-column subtile: fp16 numerators e = fp16(e^(x - m_u)) (0 past V,
+    shape [rows, nsub*64]) and partials (m_u, s_u) float32 [rows, nsub, 2] —
+    what the head GEMM epilogue writes."""
+    x = np.ascontiguousarray(logits, dtype=np.float16)
+    if x.ndim == 1:
+        x = x[None]
+    rows, V = x.shape
+    nsub = (V + SUBTILE - 1) // SUBTILE
+    e16 = np.empty((rows, nsub * SUBTILE), dtype=np.float16)
+    ms = np.empty((rows, nsub, 2), dtype=np.float32)
+    for r in range(rows):
+        lib().oc_softmax_parts(_p(x) + r * V * 2, V, _p(e16) + r * nsub * SUBTILE * 2,
+                               _p(ms) + r * nsub * 8)
+    return e16, ms
 
 
 def cdf_from_probs(probs: np.ndarray, bits: int) -> np.ndarray:

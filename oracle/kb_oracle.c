@@ -10,17 +10,29 @@
  *     reference itself produced (tests/golden/).
  *  2. The probability -> integer CDF rule of krunch_ac/cdf.py:22-74
  *     (count = floor(p*(T-V))+1, deficit to the argmax, smallest index on
- *     ties), evaluated in the fixed order the GPU kernel uses so that the
- *     result is bit-identical to it:
- *       - NT = 512 virtual threads, thread t owns [t*L, min((t+1)*L, V)),
- *         L = ceil(V/NT), and sums its segment left to right;
- *       - partials meet in a xor butterfly over 32 lanes (offsets 16..1),
- *         then the same butterfly over the 16 warp results (zero padded);
- *       - exp is oc_expf below (the same algorithm as the kernel's kb_expf).
- *     The numpy reference (cdf.py) sums in numpy's pairwise order, so it can
- *     differ from this in the last bit of a sum and hence by +-1 in rare
- *     counts; tests compare against it with that allowance and against this
- *     file bit for bit.
+ *     ties), evaluated in the fixed order the GPU kernels use so that the
+ *     result is bit-identical to them.
+ *     From logits (fp16 row x, V valid columns), per 64-column subtile u
+ *     [64u, min(64u+64, V)): m_u = max x_i; e_i = fp16(e^(x_i - m_u)); s_u =
+ *     sum of e_i left to right.  The normaliser (M, S) merges the (m_u, s_u):
+ *     virtual thread t of 512 merges u = t, t+512, ... in order; each warp of
+ *     32 threads combines in a xor butterfly (16..1); the 16 warp results,
+ *     padded to 32 with the neutral (-inf, 0), combine in the same butterfly.
+ *     merge keeps the larger max and adds the other sum scaled by
+ *     e^(m_small - m_large) (ties: plain sum), which is symmetric, so every
+ *     butterfly lane gets the same value.  Then with scale = T - V,
+ *       gs_u = (e^(m_u - M) * (1/S)) * scale,   q_i = e_i * gs_u,
+ *       c_i  = floor(q_i) + 1,   argmax = smallest i with the largest q_i.
+ *     exp is oc_expf below (the same algorithm as the kernels' kb_expf).
+ *     The head GEMM's epilogue produces e_i and (m_u, s_u) as it computes the
+ *     logits; the CDF kernels derive them when given raw logits.
+ *     From probabilities the row sum uses NT = 512 virtual threads, thread t
+ *     summing [t*L, min((t+1)*L, V)), L = ceil(V/NT), left to right, then a
+ *     xor butterfly over 32 lanes and the same over the 16 warp results;
+ *     p_i = x_i / S, c_i = floor(p_i * (T-V)) + 1, argmax over p_i.
+ *     numpy's pairwise sum (cdf.py) can differ from these orders in a last
+ *     bit, hence by +-1 in rare counts; tests compare against cdf.py with
+ *     that allowance and against this file bit for bit.
  *
  * Build: gcc -O2 -fPIC -shared -ffp-contract=off -fno-fast-math (see build.py)
  */
@@ -50,25 +62,50 @@ float oc_half_to_float(uint16_t h) {
     return bits_f(s | ((e + 112) << 23) | (m << 13));
 }
 
-/* Cody-Waite reduction with a 12-bit ln2 head; degree-6 Taylor polynomial;
- * 2^n through the exponent field.  Same algorithm and constants as the
+/* fp32 -> fp16 bits, round to nearest even (IEEE). */
+uint16_t oc_float_to_half(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const int exp = (int)((x >> 23) & 0xff);
+    uint32_t mant = x & 0x7fffffu;
+    if (exp == 255) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    const int e = exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (exp == 0) return (uint16_t)sign;
+        const int shift = 126 - exp; /* bits dropped from the 24-bit significand */
+        if (shift > 24) return (uint16_t)sign;
+        mant |= 0x800000u;
+        uint32_t h = mant >> shift;
+        const uint32_t rem = mant & ((1u << shift) - 1u), half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (h & 1u))) ++h;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = ((uint32_t)e << 10) | (mant >> 13);
+    const uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+}
+
+/* e^x = 2^(x*log2e): n = rint(y), f = y - n, degree-5 Taylor polynomial of
+ * 2^f, n added to the exponent field.  Same algorithm and constants as the
  * kernel-side kb_expf; every operation is a single IEEE rounding. */
 float oc_expf(float x) {
     if (!(x >= -86.0f)) return 0.0f;
-    const float LOG2E = bits_f(0x3fb8aa3bu);
-    const float LN2_HI = bits_f(0x3f317000u);
-    const float LN2_LO = bits_f(0x3805fdf4u);
-    const float n = rintf(x * LOG2E);
-    float r = fmaf(-n, LN2_HI, x);
-    r = fmaf(-n, LN2_LO, r);
-    float p = 1.0f / 720.0f;
-    p = fmaf(p, r, 1.0f / 120.0f);
-    p = fmaf(p, r, 1.0f / 24.0f);
-    p = fmaf(p, r, 1.0f / 6.0f);
-    p = fmaf(p, r, 0.5f);
-    p = fmaf(p, r, 1.0f);
-    p = fmaf(p, r, 1.0f);
-    return p * bits_f((uint32_t)((int)n + 127) << 23);
+    const float y = x * bits_f(0x3fb8aa3bu);
+    const float n = rintf(y);
+    const float f = y - n;
+    float p = bits_f(0x3aaec3ffu);
+    p = fmaf(p, f, bits_f(0x3c1d955bu));
+    p = fmaf(p, f, bits_f(0x3d635847u));
+    p = fmaf(p, f, bits_f(0x3e75fdf0u));
+    p = fmaf(p, f, bits_f(0x3f317218u));
+    p = fmaf(p, f, 1.0f);
+    uint32_t u;
+    memcpy(&u, &p, 4);
+    u += (uint32_t)((int32_t)n * (1 << 23));
+    return bits_f(u);
 }
 
 static float butterfly32(float* v) {
@@ -94,56 +131,133 @@ static float tree_sum(const float* part) {
 /* ------------------------------------------------------------------------- */
 /* CDF                                                                       */
 /* ------------------------------------------------------------------------- */
-/* p_i source: 0 = fp16 logits (softmax), 1 = fp32 probabilities. */
+typedef struct {
+    float m, s;
+} ms_t;
+
+static ms_t ms_merge(ms_t a, ms_t b) {
+    ms_t r;
+    if (a.m >= b.m) {
+        r.m = a.m;
+        r.s = a.s + b.s * oc_expf(b.m - a.m);
+    } else {
+        r.m = b.m;
+        r.s = b.s + a.s * oc_expf(a.m - b.m);
+    }
+    return r;
+}
+
+#define OC_SUB 64
+
+/* Subtile numerators e_i (fp16 bits, 0 past V) and partials (m_u, s_u) of a
+ * row of V fp16 logits: e16 has ceil(V/64)*64 entries, ms 2*ceil(V/64). */
+void oc_softmax_parts(const uint16_t* logits, int V, uint16_t* e16, float* ms) {
+    const int nsub = (V + OC_SUB - 1) / OC_SUB;
+    for (int u = 0; u < nsub; ++u) {
+        const int a = u * OC_SUB, e = a + OC_SUB < V ? a + OC_SUB : V;
+        float m = -INFINITY, s = 0.0f;
+        for (int i = a; i < e; ++i) {
+            const float x = oc_half_to_float(logits[i]);
+            if (x > m) m = x;
+        }
+        for (int i = a; i < a + OC_SUB; ++i) {
+            if (i < e) {
+                e16[i] = oc_float_to_half(oc_expf(oc_half_to_float(logits[i]) - m));
+                s = s + oc_half_to_float(e16[i]);
+            } else {
+                e16[i] = 0;
+            }
+        }
+        ms[2 * u] = m;
+        ms[2 * u + 1] = s;
+    }
+}
+
+/* Row normaliser (M, S) from the subtile partials, in the kernels' order. */
+static ms_t row_normaliser(const float* ms, int nsub) {
+    ms_t th[OC_NT];
+    ms_t w[32], t[32];
+    for (int i = 0; i < OC_NT; ++i) {
+        ms_t acc = {-INFINITY, 0.0f};
+        for (int u = i; u < nsub; u += OC_NT) {
+            ms_t p = {ms[2 * u], ms[2 * u + 1]};
+            acc = ms_merge(acc, p);
+        }
+        th[i] = acc;
+    }
+    for (int k = 0; k < OC_NW; ++k) {
+        ms_t* v = th + 32 * k;
+        for (int off = 16; off > 0; off >>= 1) {
+            for (int i = 0; i < 32; ++i) t[i] = ms_merge(v[i], v[i ^ off]);
+            memcpy(v, t, sizeof(t));
+        }
+        w[k] = v[0];
+    }
+    for (int k = OC_NW; k < 32; ++k) {
+        w[k].m = -INFINITY;
+        w[k].s = 0.0f;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        for (int i = 0; i < 32; ++i) t[i] = ms_merge(w[i], w[i ^ off]);
+        memcpy(w, t, sizeof(t));
+    }
+    return w[0];
+}
+
+/* source: 0 = fp16 logits (softmax), 1 = fp32 probabilities. */
 static void cdf_row(const void* src, int kind, int V, int bits, int32_t* out) {
-    const int L = (V + OC_NT - 1) / OC_NT;
     const int64_t T = (int64_t)1 << bits;
     const float scale = (float)(T - V);
-    float* vals = (float*)malloc(sizeof(float) * (size_t)V);
-    float part[OC_NT];
-    float m = -INFINITY, inv = 0.0f, S = 0.0f;
+    float* q = (float*)malloc(sizeof(float) * (size_t)V);  /* q_i (logits) or p_i (probs) */
+    int64_t total = 0;
+    int amax = -1;
+    float best = -INFINITY;
 
     if (kind == 0) {
         const uint16_t* x = (const uint16_t*)src;
+        const int nsub = (V + OC_SUB - 1) / OC_SUB;
+        float* ms = (float*)malloc(sizeof(float) * 2 * (size_t)nsub);
+        uint16_t* e16 = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nsub * OC_SUB);
+        oc_softmax_parts(x, V, e16, ms);
+        const ms_t n = row_normaliser(ms, nsub);
+        const float inv = 1.0f / n.s;
+        for (int u = 0; u < nsub; ++u) {
+            const float gs = (oc_expf(ms[2 * u] - n.m) * inv) * scale;
+            const int a = u * OC_SUB, e = a + OC_SUB < V ? a + OC_SUB : V;
+            for (int i = a; i < e; ++i) q[i] = oc_half_to_float(e16[i]) * gs;
+        }
+        free(ms);
+        free(e16);
         for (int i = 0; i < V; ++i) {
-            vals[i] = oc_half_to_float(x[i]);
-            if (vals[i] > m) m = vals[i];
+            const int c = (int)floorf(q[i]) + 1;
+            out[i + 1] = c;
+            total += c;
+            if (q[i] > best) { best = q[i]; amax = i; }
         }
-        for (int t = 0; t < OC_NT; ++t) {
-            int a = t * L < V ? t * L : V, e = a + L < V ? a + L : V;
-            float s = 0.0f;
-            for (int i = a; i < e; ++i) s = s + oc_expf(vals[i] - m);
-            part[t] = s;
-        }
-        S = tree_sum(part);
-        inv = 1.0f / S;
     } else {
         const float* x = (const float*)src;
+        const int L = (V + OC_NT - 1) / OC_NT;
+        float part[OC_NT];
         for (int t = 0; t < OC_NT; ++t) {
             int a = t * L < V ? t * L : V, e = a + L < V ? a + L : V;
             float s = 0.0f;
             for (int i = a; i < e; ++i) s = s + x[i];
             part[t] = s;
         }
-        S = tree_sum(part);
+        float S = tree_sum(part);
         if (S < 1e-30f) S = 1e-30f;
-        memcpy(vals, x, sizeof(float) * (size_t)V);
-    }
-
-    int64_t total = 0;
-    int amax = -1;
-    float bp = -INFINITY;
-    for (int i = 0; i < V; ++i) {
-        const float p = kind == 0 ? oc_expf(vals[i] - m) * inv : vals[i] / S;
-        const int c = (int)floorf(p * scale) + 1;
-        out[i + 1] = c;
-        total += c;
-        if (p > bp) { bp = p; amax = i; }
+        for (int i = 0; i < V; ++i) {
+            const float p = x[i] / S;
+            const int c = (int)floorf(p * scale) + 1;
+            out[i + 1] = c;
+            total += c;
+            if (p > best) { best = p; amax = i; }
+        }
     }
     out[amax + 1] += (int32_t)(T - total);
     out[0] = 0;
     for (int i = 1; i <= V; ++i) out[i] += out[i - 1];
-    free(vals);
+    free(q);
 }
 
 void oc_cdf_from_logits(const uint16_t* logits, int64_t stride, int rows, int V, int bits,

@@ -35,7 +35,7 @@ def test_host_only_calls():
     assert lib.kb_status_string(-2) == b"unsupported shape"
     # argument validation happens before any device work
     assert lib.kb_gemm(0, None, 0, None, 0, 1, 128, 64, 0, None, 128, None, None, None) == -1
-    assert lib.kb_cdf_rows(None, 0, 1, 10, 16, 0, None, None, None) == -1
+    assert lib.kb_cdf_rows(None, 0, 1, 10, 16, 0, None, 0, None, None, None) == -1
     assert lib.kb_coder_encode_lohi(None, 1, 1, None, 16, None, 0, None, None, None) == -1
     h = ctypes.c_void_p()
     d = N.ModelDesc()

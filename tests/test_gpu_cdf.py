@@ -26,11 +26,11 @@ def _cdf_gpu(torch, logits_np, bits, mode=1, stride=None, symbols=None):
     if mode == N.KB_CDF_LOHI:
         out = torch.empty((rows, 2), dtype=torch.int32, device="cuda")
         sym = torch.from_numpy(symbols.astype(np.int32)).cuda()
-        N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, sym.data_ptr(),
+        N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, None, 0, sym.data_ptr(),
                out.data_ptr(), N.stream_ptr())
         return out.cpu().numpy().view(np.uint32)
     out = torch.empty((rows, V + 1), dtype=torch.int32, device="cuda")
-    N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, None, out.data_ptr(),
+    N.call("kb_cdf_rows", x.data_ptr(), stride, rows, V, bits, mode, None, 0, None, out.data_ptr(),
            N.stream_ptr())
     return out.cpu().numpy()
 
@@ -112,7 +112,8 @@ def test_fused_decode_step_roundtrip(torch, bits):
     for t in range(T):
         lg[:, :V] = logits[t]
         x = torch.from_numpy(lg).cuda()
-        N.call("kb_decode_logits_step", x.data_ptr(), Vp, B, V, bits, inb.data_ptr(), inb.numel(),
+        N.call("kb_decode_logits_step", x.data_ptr(), Vp, B, V, bits, None, 0, inb.data_ptr(),
+               inb.numel(),
                offs_t.data_ptr(), st.data_ptr(), cnt.data_ptr(), cur.data_ptr(), hist.data_ptr(),
                T, sp)
     h = hist.cpu().numpy()
@@ -120,3 +121,33 @@ def test_fused_decode_step_roundtrip(torch, bits):
         assert h[b, :lens[b]].tolist() == sym[b, :lens[b]].tolist()
         assert (h[b, lens[b]:] == -1).all()
     assert cnt[:, 0].cpu().tolist() == lens
+
+
+def test_head_gemm_numerators_match_oracle(torch):
+    """The head GEMM's softmax numerators and partials == the C oracle's from
+    the raw logits, and (lo, hi) from them == (lo, hi) from the raw logits
+    == the oracle's."""
+    from krunch_b200 import _native as N
+    from krunch_b200.model import RWKVModel
+    from krunch_b200.synth import random_weights
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=4))
+    B, T, V = 3, 9, 300
+    tok = torch.from_numpy(np.random.default_rng(3).integers(0, V, (B, T)).astype(np.int32)).cuda()
+    raw, num, stats = m.new_logits(B, T), m.new_logits(B, T), m.new_stats(B, T)
+    m.forward_window(tok, m.new_state(B), m.new_workspace(B, T), raw)
+    m.forward_window(tok, m.new_state(B), m.new_workspace(B, T), num, stats)
+    raw_h = raw[:, :V].cpu().numpy()
+    e16, ms = coder.softmax_parts(raw_h)
+    nsub = ms.shape[1]
+    assert np.array_equal(num[:, :nsub * 64].cpu().numpy().view(np.uint16), e16.view(np.uint16))
+    assert np.array_equal(stats.cpu().numpy()[:, :nsub].view(np.uint32), ms.view(np.uint32))
+    sym = torch.from_numpy(np.random.default_rng(4).integers(0, V, B * T).astype(np.int32)).cuda()
+    outs = []
+    for x, st, stride in ((num, stats, m.stats_stride), (raw, None, 0)):
+        o = torch.empty((B * T, 2), dtype=torch.int32, device="cuda")
+        N.call("kb_cdf_rows", x.data_ptr(), m.spec.vocab_pad, B * T, V, 16, N.KB_CDF_LOHI,
+               None if st is None else st.data_ptr(), stride, sym.data_ptr(), o.data_ptr(),
+               N.stream_ptr())
+        outs.append(o.cpu().numpy())
+    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(outs[0].view(np.uint32), coder.lohi_from_logits(raw_h, sym.cpu().numpy(), 16))

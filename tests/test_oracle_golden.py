@@ -123,7 +123,7 @@ def test_expf_accuracy():
     x = np.linspace(-86, 0, 20001).astype(np.float32)
     e = coder.expf(x)
     ref = np.exp(x.astype(np.float64))
-    assert np.max(np.abs(e - ref) / ref) < 3e-7
+    assert np.max(np.abs(e - ref) / ref) < 7e-6
     assert coder.expf([-87.0, -np.inf])[0] == 0.0
 
 
