@@ -133,10 +133,10 @@ enum kb_cdf_mode {
 
 /* With logit_stats NULL, logits_f16 holds raw fp16 logits [rows, row_stride]
  * (V valid columns).  With logit_stats non-NULL it holds what
- * kb_forward_window writes when asked for stats: per 64-column subtile u the
+ * kb_forward_window writes when asked for stats: per 32-column subtile u the
  * fp16 numerators e^(x - m_u), and logit_stats float2 [rows, stats_stride]
  * the subtile partials (m_u, sum of the numerators), stats_stride >=
- * ceil(V / 64).  Both inputs give bit-identical CDFs (the kernel derives the
+ * ceil(V / 32).  Both inputs give bit-identical CDFs (the kernel derives the
  * numerators and partials from raw logits itself). */
 int kb_cdf_rows(const uint16_t* logits_f16, int64_t row_stride, int rows, int V,
                 int cdf_bits, int mode, const float* logit_stats, int64_t stats_stride,
@@ -246,7 +246,7 @@ size_t kb_forward_workspace_bytes(const kb_model* model, int B, int T);
 /* Packed forward of a window: tokens int32 [B, T] (inputs), state as above
  * (read and updated), logits fp16 [B*T, vocab_pad] (row b*T+t).  When
  * logit_stats is non-NULL the head writes, instead of raw logits, the softmax
- * numerators and partials kb_cdf_rows takes (stats float2 [B*T, vocab_pad/64]).
+ * numerators and partials kb_cdf_rows takes (stats float2 [B*T, vocab_pad/32]).
  * T = 1 is the stepped decompress forward; the same kernels run for every T,
  * which makes packed and stepped results bit-identical.  Replaces
  * forward_packed_window / forward_stepped_batched

@@ -6,7 +6,7 @@
 //   c_amax += T - sum(c)                         (argmax of p, smallest index on ties)
 //   cdf    = [0, cumsum(c)]
 //
-// The softmax follows softmax_stats.cuh: per 64-column subtile u a max m_u
+// The softmax follows softmax_stats.cuh: per 32-column subtile u a max m_u
 // and fp16 numerators e_i = e^(x_i - m_u); the only floating-point reduction,
 // the normaliser (M, S), merges the subtile partials in a fixed order.  With
 // gs_u = (e^(m_u - M) / S) * (T - V) a count is c_i = floor(e_i * gs_u) + 1,
@@ -215,10 +215,9 @@ __device__ __forceinline__ void row_setup(Part part, IsOne is_one, int nsub, flo
     }
     const int ustar = block_argmax(best, bu, red);  // contains __syncthreads
     if (warp == 0) {
-        const int a = ustar * SUBTILE;
+        const int a = ustar * SUBTILE;  // SUBTILE == 32: one lane per column
         const unsigned b0 = __ballot_sync(0xffffffffu, is_one(a + lane));
-        const unsigned b1 = __ballot_sync(0xffffffffu, is_one(a + 32 + lane));
-        if (lane == 0) rs.amax = b0 ? a + __ffs(b0) - 1 : a + 32 + __ffs(b1) - 1;
+        if (lane == 0) rs.amax = a + __ffs(b0) - 1;
     }
     __syncthreads();
 }
@@ -537,7 +536,7 @@ static inline bool cdf_args_ok(int V, int bits) {
 }
 
 static inline bool stats_ok(const float* stats, int64_t stats_stride, int V) {
-    // stats_stride >= number of 64-column subtiles, float2-aligned
+    // stats_stride >= number of 32-column subtiles, float2-aligned
     return !stats || (stats_stride >= (V + SUBTILE - 1) / SUBTILE &&
                       (reinterpret_cast<uintptr_t>(stats) & 7u) == 0);
 }

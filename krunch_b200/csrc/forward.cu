@@ -257,7 +257,7 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
         if (logit_stats)
             KB_TRY(launch_gemm_logits(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
                                       logits, d.vocab_pad, d.n_vocab, logit_stats,
-                                      d.vocab_pad / 64, st));
+                                      d.vocab_pad / 32, st));
         else
             KB_TRY(launch_gemm_f16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
                                    KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));

@@ -10,7 +10,7 @@
 //               64-column quarter of the tile; tcgen05.ld, the fused epilogue,
 //               16-byte stores.  Draining accumulator i overlaps the MMAs of
 //               tile i+1.  The head's epilogue stores, instead of the logits,
-//               e^(x - m_u) in fp16 for every 64-column subtile u together
+//               e^(x - m_u) in fp16 for every 32-column subtile u together
 //               with the subtile's (m_u, sum), so the CDF kernel needs no exp
 //               per element (softmax_stats.cuh).
 // Output tile (m, n) walks K from 0 to K in 64-wide blocks, 16 per MMA, for
@@ -57,6 +57,18 @@ __device__ __forceinline__ bool tc_aborted(TcBars* b) {
 }
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// Tile order: groups of TC_GROUP_M row blocks; inside a group the row block
+// changes fastest, so the CTAs running at the same time share a few weight
+// tiles (read from L2) and a few activation row blocks.
+constexpr int TC_GROUP_M = 16;
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m0, int& n0) {
+    const int per_group = TC_GROUP_M * num_n;
+    const int g = t / per_group, r = t - g * per_group;
+    const int gm = min(TC_GROUP_M, num_m - g * TC_GROUP_M);
+    m0 = (g * TC_GROUP_M + r % gm) * TC_BM;
+    n0 = (r / gm) * TC_BN;
+}
 
 // Epilogue on 32 consecutive columns [c0, c0+32) of row r.
 template <int EPI>
@@ -130,7 +142,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_n = (N + TC_BN - 1) / TC_BN;
-    const int tiles = ((M + TC_BM - 1) / TC_BM) * num_n;
+    const int num_m = (M + TC_BM - 1) / TC_BM;
+    const int tiles = num_m * num_n;
     const int KB = K / TC_BK;
 
     if (threadIdx.x == 0) {
@@ -162,7 +175,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_parity = 0;  // per-stage bit masks
             for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x) {
-                const int m0 = (t / num_n) * TC_BM, n0 = (t % num_n) * TC_BN;
+                int m0, n0;
+                tile_coords(t, num_m, num_n, m0, n0);
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1u)) {
                         tc_fail(bars, 1);
@@ -232,7 +246,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
         for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
             const int a = i & 1;
             const uint32_t use = (uint32_t)(i >> 1);
-            const int m0 = (t / num_n) * TC_BM, n0 = (t % num_n) * TC_BN;
+            int m0, n0;
+                tile_coords(t, num_m, num_n, m0, n0);
             if (!tc::mbar_wait(&bars->tfull[a], use & 1u)) {
                 tc_fail(bars, 4);
                 break;
@@ -241,8 +256,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
             const int64_t row = m0 + q * 32 + lane;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * TC_BN);
             if (EPI == KB_EPI_LOGITS_STATS) {
-                // pass 1: subtile max of the fp16-rounded logits (columns < V)
-                float m = -INFINITY;
+                // one pass per 32-column subtile: max of the fp16-rounded
+                // logits (columns < V), e = fp16(e^(x - m)), left-to-right sum
 #pragma unroll 1
                 for (int c = 2 * g; c < 2 * g + 2; ++c) {
                     const int col0 = n0 + c * 32;
@@ -250,32 +265,44 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     uint32_t v[32];
                     tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
                     tc::tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (col0 + j < V) m = fmaxf(m, __half2float(__float2half_rn(u2f(v[j]))));
-                }
-                // pass 2: e = fp16(e^(x - m)), left-to-right sum, store e
-                float s = 0.0f;
-#pragma unroll 1
-                for (int c = 2 * g; c < 2 * g + 2; ++c) {
-                    const int col0 = n0 + c * 32;
-                    if (col0 >= N) break;
-                    uint32_t v[32];
-                    tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
-                    tc::tmem_ld_wait();
-                    uint32_t packed[16];
+                    float xr[32];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
-                        uint16_t e0 = 0, e1 = 0;
-                        if (col0 + j < V) {
-                            e0 = exp_rel_f16(__half2float(__float2half_rn(u2f(v[j]))), m);
+                        const float2 f = __half22float2(__floats2half2_rn(u2f(v[j]), u2f(v[j + 1])));
+                        xr[j] = f.x;
+                        xr[j + 1] = f.y;
+                    }
+                    const int nv = V - col0;  // valid columns in this subtile
+                    float m = -INFINITY, s = 0.0f;
+                    uint32_t packed[16];
+                    if (nv >= 32) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) m = fmaxf(m, xr[j]);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            const uint16_t e0 = exp_rel_f16(xr[j], m);
+                            const uint16_t e1 = exp_rel_f16(xr[j + 1], m);
                             s = __fadd_rn(s, h2f(e0));
-                        }
-                        if (col0 + j + 1 < V) {
-                            e1 = exp_rel_f16(__half2float(__float2half_rn(u2f(v[j + 1]))), m);
                             s = __fadd_rn(s, h2f(e1));
+                            packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
                         }
-                        packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nv) m = fmaxf(m, xr[j]);
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            uint16_t e0 = 0, e1 = 0;
+                            if (j < nv) {
+                                e0 = exp_rel_f16(xr[j], m);
+                                s = __fadd_rn(s, h2f(e0));
+                            }
+                            if (j + 1 < nv) {
+                                e1 = exp_rel_f16(xr[j + 1], m);
+                                s = __fadd_rn(s, h2f(e1));
+                            }
+                            packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
+                        }
                     }
                     if (row < M) {
                         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) +
@@ -284,10 +311,10 @@ __global__ void __launch_bounds__(TC_NT, 1)
                         for (int j = 0; j < 4; ++j)
                             dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
                                                 packed[4 * j + 3]);
+                        const int u = col0 / SUBTILE;
+                        if (u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
                     }
                 }
-                const int u = (n0 + 64 * g) / SUBTILE;
-                if (row < M && u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
             } else {
 #pragma unroll 1
                 for (int c = 2 * g; c < 2 * g + 2; ++c) {

@@ -30,7 +30,7 @@ int launch_gemm_f16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t l
 int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
                    int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
                    const uint16_t* gate, cudaStream_t st);
-// Head GEMM: per row and 64-column subtile u, out holds fp16 e^(x - m_u) of
+// Head GEMM: per row and 32-column subtile u, out holds fp16 e^(x - m_u) of
 // the fp16-rounded logits x (0 past column V) and stats[row * stats_stride + u]
 // = (m_u, sum of those e), as defined in softmax_stats.cuh.
 constexpr int KB_EPI_LOGITS_STATS = 6;

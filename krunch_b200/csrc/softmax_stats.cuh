@@ -1,8 +1,8 @@
 // Softmax pieces shared by the head GEMM epilogue (gemm_tc.cu) and the CDF
 // kernels (cdf.cu).
 //
-// A logits row x (fp16 values) is cut into 64-column subtiles.  For subtile u
-// with columns [64u, min(64u+64, V)):
+// A logits row x (fp16 values) is cut into 32-column subtiles.  For subtile u
+// with columns [32u, min(32u+32, V)):
 //   m_u  = max x_i
 //   e_i  = fp16(kb_expf(x_i - m_u))                  (stored by the head GEMM)
 //   s_u  = sum_i e_i, left to right in fp32
@@ -21,7 +21,8 @@
 
 namespace kb {
 
-constexpr int SUBTILE = 64;  // columns per softmax partial
+constexpr int SUBTILE = 32;  // columns per softmax partial (one TMEM load)
+static_assert(SUBTILE == 32, "the CDF argmax search takes one warp ballot per subtile");
 
 struct MS {
     float m, s;

@@ -147,8 +147,8 @@ class RWKVModel:
 
     @property
     def stats_stride(self) -> int:
-        """Softmax partials per logits row (one per 64 head columns)."""
-        return self.spec.vocab_pad // 64
+        """Softmax partials per logits row (one per 32 head columns)."""
+        return self.spec.vocab_pad // 32
 
     def new_stats(self, B: int, T: int) -> torch.Tensor:
         return torch.empty((B * T, self.stats_stride, 2), dtype=torch.float32, device=self.device)
@@ -158,7 +158,7 @@ class RWKVModel:
         """tokens int32 [B, T] (contiguous, on device) -> logits fp16 [B*T, vocab_pad].
 
         ``state`` is read and advanced in place.  With ``stats`` (from
-        new_stats) the head writes, instead of raw logits, the per-64-column
+        new_stats) the head writes, instead of raw logits, the per-32-column
         softmax numerators into ``logits`` and their partials into ``stats``
         (the input kb_cdf_rows / kb_decode_logits_step take)."""
         B, T = tokens.shape

@@ -100,11 +100,11 @@ def lohi_from_logits(logits: np.ndarray, symbols: np.ndarray, bits: int,
     return out
 
 
-SUBTILE = 64
+SUBTILE = 32
 
 
 def softmax_parts(logits: np.ndarray):
-    """Per 64-column subtile: fp16 numerators e = fp16(e^(x - m_u)) (0 past V,
+    """Per 32-column subtile: fp16 numerators e = fp16(e^(x - m_u)) (0 past V,
     shape [rows, nsub*64]) and partials (m_u, s_u) float32 [rows, nsub, 2] —
     what the head GEMM epilogue writes."""
     x = np.ascontiguousarray(logits, dtype=np.float16)

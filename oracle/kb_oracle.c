@@ -12,8 +12,8 @@
  *     (count = floor(p*(T-V))+1, deficit to the argmax, smallest index on
  *     ties), evaluated in the fixed order the GPU kernels use so that the
  *     result is bit-identical to them.
- *     From logits (fp16 row x, V valid columns), per 64-column subtile u
- *     [64u, min(64u+64, V)): m_u = max x_i; e_i = fp16(e^(x_i - m_u)); s_u =
+ *     From logits (fp16 row x, V valid columns), per 32-column subtile u
+ *     [32u, min(32u+32, V)): m_u = max x_i; e_i = fp16(e^(x_i - m_u)); s_u =
  *     sum of e_i left to right.  The normaliser (M, S) merges the (m_u, s_u):
  *     virtual thread t of 512 merges u = t, t+512, ... in order; each warp of
  *     32 threads combines in a xor butterfly (16..1); the 16 warp results,
@@ -147,10 +147,10 @@ static ms_t ms_merge(ms_t a, ms_t b) {
     return r;
 }
 
-#define OC_SUB 64
+#define OC_SUB 32
 
 /* Subtile numerators e_i (fp16 bits, 0 past V) and partials (m_u, s_u) of a
- * row of V fp16 logits: e16 has ceil(V/64)*64 entries, ms 2*ceil(V/64). */
+ * row of V fp16 logits: e16 has ceil(V/32)*32 entries, ms 2*ceil(V/32). */
 void oc_softmax_parts(const uint16_t* logits, int V, uint16_t* e16, float* ms) {
     const int nsub = (V + OC_SUB - 1) / OC_SUB;
     for (int u = 0; u < nsub; ++u) {

@@ -139,7 +139,7 @@ def test_head_gemm_numerators_match_oracle(torch):
     raw_h = raw[:, :V].cpu().numpy()
     e16, ms = coder.softmax_parts(raw_h)
     nsub = ms.shape[1]
-    assert np.array_equal(num[:, :nsub * 64].cpu().numpy().view(np.uint16), e16.view(np.uint16))
+    assert np.array_equal(num[:, :nsub * 32].cpu().numpy().view(np.uint16), e16.view(np.uint16))
     assert np.array_equal(stats.cpu().numpy()[:, :nsub].view(np.uint32), ms.view(np.uint32))
     sym = torch.from_numpy(np.random.default_rng(4).integers(0, V, B * T).astype(np.int32)).cuda()
     outs = []
