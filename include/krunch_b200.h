@@ -186,6 +186,36 @@ int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
             int M, int N, int K, int epilogue, void* out, int64_t ldo,
             const uint16_t* resid, const uint16_t* gate, void* stream);
 
+/* w8a8 GEMM: A int8 [M, lda] with a fp32 dequantisation factor per row
+ * (a_scale [M]), W int8 [N, ldw] with a fp16 factor per row of W (w_scale
+ * [N], per output channel).  Exact int32 accumulation (tcgen05 kind::i8), then
+ * y = (acc * a_scale[m]) * w_scale[n] and the epilogue as in kb_gemm.  Any
+ * tiling gives the same bits.  Requires K % 128 == 0, N % 32 == 0.  The
+ * reference's int8 GEMM is w8a16 (det_matmul_tc_uint8.cu:43-254); this is the
+ * w8a8 scheme with per-output-channel scales. */
+int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t* W,
+               int64_t ldw, const uint16_t* w_scale, int M, int N, int K, int epilogue,
+               void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
+               int tile_n, void* stream);
+
+/* Per-output-channel int8 weight quantisation of fp16 W [N, K]:
+ * scale[n] = fp16(max_k |W[n,k]| / 127), q = clamp(rint(W / scale), -127, 127). */
+int kb_quantize_weight(const uint16_t* w, int N, int K, int8_t* q, uint16_t* scale,
+                       void* stream);
+
+/* Per-row int8 activation quantisation of fp16 x [R, K] (K % 8 == 0):
+ * amax = max |x[r,:]|, q = clamp(rint(x * (127 / amax)), -127, 127),
+ * scale[r] = amax / 127 (fp32; 0 for an all-zero row). */
+int kb_quantize_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, void* stream);
+
+/* kb_gemm with the output tile width fixed: tile_n in {32, 64, 128, 256}, or
+ * 0 for the library's choice (the widest width whose tiles fill the SMs).
+ * Every width gives bit-identical results: an output element's K walk does
+ * not depend on the tile shape. */
+int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
+                  int M, int N, int K, int epilogue, void* out, int64_t ldo,
+                  const uint16_t* resid, const uint16_t* gate, int tile_n, void* stream);
+
 /* Device-side failure report of the tcgen05 kernels: every mbarrier wait in
  * them is bounded, and a wait that expires records an error and makes the
  * kernel unwind (no hang).  Returns KB_OK or KB_ERR_TIMEOUT (KB_ERR_CUDA if the
@@ -211,6 +241,10 @@ typedef struct kb_layer_desc {
     const void* ffn_kw;  /* [F,C] */
     const void* ffn_vw;  /* [C,F] */
     const void* ffn_rw;  /* [C,C] */
+    /* KB_I8 only: fp16 dequantisation factor per output channel (per row of
+     * the K-major matrix above), 16-byte aligned; NULL for KB_F16. */
+    const uint16_t* att_ks; const uint16_t* att_vs; const uint16_t* att_rs; const uint16_t* att_os;
+    const uint16_t* ffn_ks; const uint16_t* ffn_vs; const uint16_t* ffn_rs;
 } kb_layer_desc;
 
 typedef struct kb_model_desc {
@@ -222,6 +256,7 @@ typedef struct kb_model_desc {
     const float* ln_out_w; const float* ln_out_b;
     const void* head;    /* [vocab_pad, C] K-major, rows >= n_vocab zero       */
     const kb_layer_desc* layers; /* n_layer entries (copied at create)        */
+    const uint16_t* head_scale;  /* KB_I8: fp16 [vocab_pad] factors, else NULL  */
 } kb_model_desc;
 
 typedef struct kb_model kb_model;

@@ -31,14 +31,15 @@ class LayerDesc(C.Structure):
         "ln1_w", "ln1_b", "ln2_w", "ln2_b",
         "att_mix_k", "att_mix_v", "att_mix_r", "att_decay", "att_first",
         "att_kw", "att_vw", "att_rw", "att_ow",
-        "ffn_mix_k", "ffn_mix_r", "ffn_kw", "ffn_vw", "ffn_rw")]
+        "ffn_mix_k", "ffn_mix_r", "ffn_kw", "ffn_vw", "ffn_rw",
+        "att_ks", "att_vs", "att_rs", "att_os", "ffn_ks", "ffn_vs", "ffn_rs")]
 
 
 class ModelDesc(C.Structure):
     _fields_ = [("n_layer", i32), ("n_embd", i32), ("n_ffn", i32), ("n_vocab", i32),
                 ("vocab_pad", i32), ("wdtype", i32), ("wkv_convention", i32),
                 ("emb", vp), ("ln_out_w", vp), ("ln_out_b", vp), ("head", vp),
-                ("layers", C.POINTER(LayerDesc))]
+                ("layers", C.POINTER(LayerDesc)), ("head_scale", vp)]
 
 
 # name -> (restype, argtypes); mirrors include/krunch_b200.h
@@ -60,6 +61,10 @@ SIGNATURES = {
     "kb_decode_logits_step": (i32, [vp, i64, i32, i32, i32, vp, i64, vp, i64, vp, vp, vp, vp, vp, i64, vp]),
     "kb_device_error_status": (i32, [i32]),
     "kb_gemm": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, vp]),
+    "kb_gemm_i8": (i32, [vp, i64, vp, vp, i64, vp, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),
+    "kb_quantize_weight": (i32, [vp, i32, i32, vp, vp, vp]),
+    "kb_quantize_rows": (i32, [vp, i32, i32, vp, vp, vp]),
+    "kb_gemm_tiled": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),
     "kb_model_create": (i32, [C.POINTER(ModelDesc), C.POINTER(vp)]),
     "kb_model_destroy": (None, [vp]),
     "kb_prepare_decay": (i32, [vp, vp, i32, vp]),

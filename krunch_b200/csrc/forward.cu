@@ -111,7 +111,9 @@ extern "C" int kb_model_create(const kb_model_desc* d, kb_model** out) {
     if (d->n_layer < 1 || C < 128 || F < 128 || d->n_vocab < 2) return KB_ERR_ARG;
     if (C % 128 || F % 128 || C > 4096) return KB_ERR_SHAPE;
     if (d->vocab_pad < d->n_vocab || d->vocab_pad % 128 || d->n_vocab > 65536) return KB_ERR_SHAPE;
-    if (d->wdtype != KB_F16) return KB_ERR_UNSUPPORTED;
+    if (d->wdtype != KB_F16 && d->wdtype != KB_I8) return KB_ERR_UNSUPPORTED;
+    const bool i8 = d->wdtype == KB_I8;
+    if (i8 && !al16(d->head_scale)) return KB_ERR_ALIGN;
     if (d->wkv_convention != KB_WKV_STEP_REF && d->wkv_convention != KB_WKV_PRODUCTION)
         return KB_ERR_ARG;
     if (!al16(d->emb) || !d->ln_out_w || !d->ln_out_b || !al16(d->head) || !d->layers)
@@ -123,6 +125,9 @@ extern "C" int kb_model_create(const kb_model_desc* d, kb_model** out) {
             return KB_ERR_ARG;
         if (!al16(L.att_kw) || !al16(L.att_vw) || !al16(L.att_rw) || !al16(L.att_ow) ||
             !al16(L.ffn_kw) || !al16(L.ffn_vw) || !al16(L.ffn_rw))
+            return KB_ERR_ALIGN;
+        if (i8 && (!al16(L.att_ks) || !al16(L.att_vs) || !al16(L.att_rs) || !al16(L.att_os) ||
+                   !al16(L.ffn_ks) || !al16(L.ffn_vs) || !al16(L.ffn_rs)))
             return KB_ERR_ALIGN;
     }
     kb_model* m = new (std::nothrow) kb_model;
@@ -146,6 +151,9 @@ namespace {
 struct Workspace {
     uint16_t *x, *kx, *vx, *rx, *r, *ry, *kk;
     float *k, *v, *xx_att, *xx_ffn;
+    // w8a8 operands (KB_I8 models only): int8 rows and per-row factors
+    int8_t *q_kx, *q_vx, *q_rx, *q_ry, *q_kk;
+    float *s_kx, *s_vx, *s_rx, *s_ry, *s_kk;
 };
 
 inline size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -170,6 +178,21 @@ size_t layout(const kb_model_desc& d, int B, int T, char* base, Workspace* w) {
     t.v = (float*)take(R * C * 4);
     t.xx_att = (float*)take((size_t)B * C * 4);
     t.xx_ffn = (float*)take((size_t)B * C * 4);
+    if (d.wdtype == KB_I8) {
+        t.q_kx = (int8_t*)take(R * C);
+        t.q_vx = (int8_t*)take(R * C);
+        t.q_rx = (int8_t*)take(R * C);
+        t.q_ry = (int8_t*)take(R * C);
+        t.q_kk = (int8_t*)take(R * F);
+        t.s_kx = (float*)take(R * 4);
+        t.s_vx = (float*)take(R * 4);
+        t.s_rx = (float*)take(R * 4);
+        t.s_ry = (float*)take(R * 4);
+        t.s_kk = (float*)take(R * 4);
+    } else {
+        t.q_kx = t.q_vx = t.q_rx = t.q_ry = t.q_kk = nullptr;
+        t.s_kx = t.s_vx = t.s_rx = t.s_ry = t.s_kk = nullptr;
+    }
     if (w) *w = t;
     return off;
 }
@@ -201,11 +224,23 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
     const int R = B * T;
     const size_t BC = (size_t)B * C;
 
-    const double bpe = 2.0;  // fp16 bytes per element
+    const bool i8 = d.wdtype == KB_I8;
+    const double bpe = 2.0;  // fp16 bytes per activation element
     auto gemm = [&](const uint16_t* A, const void* W, int M, int Nn, int K, int epi, void* out,
                     const uint16_t* resid, const uint16_t* gate, int phase) -> int {
         ProfScope ps(phase, st, 2.0 * M * (double)Nn * K);
-        return launch_gemm_f16(A, K, (const uint16_t*)W, K, M, Nn, K, epi, out, Nn, resid, gate, st);
+        return launch_gemm_tc(A, K, (const uint16_t*)W, K, M, Nn, K, epi, out, Nn, resid, gate, st);
+    };
+    auto gemm8 = [&](const int8_t* A, const float* sa, const void* W, const uint16_t* sw, int M,
+                     int Nn, int K, int epi, void* out, const uint16_t* resid,
+                     const uint16_t* gate, int phase) -> int {
+        ProfScope ps(phase, st, 2.0 * M * (double)Nn * K);
+        return launch_gemm_i8(A, K, sa, (const int8_t*)W, K, sw, M, Nn, K, epi, out, Nn, resid,
+                              gate, st);
+    };
+    auto quant = [&](const uint16_t* x, int K, int8_t* q, float* qs) -> int {
+        ProfScope ps(PH_LN_MIX, st, (double)R * K * 3.0);
+        return launch_quant_rows(x, R, K, q, qs, st);
     };
     {
         ProfScope ps(PH_EMBED, st, (double)R * C * 2 * bpe);
@@ -218,49 +253,81 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
               *s_ffn = s + 4 * BC;
 
         // ---- time mix -------------------------------------------------------
-        MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx}};
+        MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx},
+                   {w.q_kx, w.q_vx, w.q_rx}, {w.s_kx, w.s_vx, w.s_rx}};
         {
-            ProfScope ps(PH_LN_MIX, st, (double)R * C * 4 * bpe);
+            ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? 2 * bpe + 3 : 4 * bpe));
             KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
         }
-        KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        if (i8) {
+            KB_TRY(gemm8(w.q_kx, w.s_kx, L.att_kw, L.att_ks, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm8(w.q_vx, w.s_vx, L.att_vw, L.att_vs, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm8(w.q_rx, w.s_rx, L.att_rw, L.att_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        } else {
+            KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        }
         {
             ProfScope ps(PH_WKV, st, (double)R * C * 12.0);
             KB_TRY(launch_wkv(d.wkv_convention, B, T, C, w.k, w.v, w.r, L.att_decay, L.att_first,
                               s_aa, s_bb, s_pp, w.ry, st));
         }
-        KB_TRY(gemm(w.ry, L.att_ow, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+        if (i8) {
+            KB_TRY(quant(w.ry, C, w.q_ry, w.s_ry));
+            KB_TRY(gemm8(w.q_ry, w.s_ry, L.att_ow, L.att_os, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+        } else {
+            KB_TRY(gemm(w.ry, L.att_ow, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+        }
         if (cudaMemcpyAsync(s_att, w.xx_att, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
             return launch_status();
 
         // ---- channel mix ----------------------------------------------------
-        MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr}};
+        MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr},
+                   {w.q_kx, w.q_rx, nullptr}, {w.s_kx, w.s_rx, nullptr}};
         {
-            ProfScope ps(PH_LN_MIX, st, (double)R * C * 3 * bpe);
+            ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 2 : 3 * bpe));
             KB_TRY(launch_ln_mix(2, w.x, B, T, C, L.ln2_w, L.ln2_b, mf, s_ffn, w.xx_ffn, nullptr, st));
         }
-        KB_TRY(gemm(w.rx, L.ffn_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.kx, L.ffn_kw, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.kk, L.ffn_vw, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+        if (i8) {
+            KB_TRY(gemm8(w.q_rx, w.s_rx, L.ffn_rw, L.ffn_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm8(w.q_kx, w.s_kx, L.ffn_kw, L.ffn_ks, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
+            KB_TRY(quant(w.kk, F, w.q_kk, w.s_kk));
+            KB_TRY(gemm8(w.q_kk, w.s_kk, L.ffn_vw, L.ffn_vs, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+        } else {
+            KB_TRY(gemm(w.rx, L.ffn_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm(w.kx, L.ffn_kw, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
+            KB_TRY(gemm(w.kk, L.ffn_vw, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+        }
         if (cudaMemcpyAsync(s_ffn, w.xx_ffn, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
             return launch_status();
     }
-    MixArgs none{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr}};
+    MixArgs none{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr},
+                 {w.q_kx, nullptr, nullptr}, {w.s_kx, nullptr, nullptr}};
     {
-        ProfScope ps(PH_LN_MIX, st, (double)R * C * 2 * bpe);
-        KB_TRY(launch_ln_mix(0, w.x, B, T, C, d.ln_out_w, d.ln_out_b, none, nullptr, nullptr, w.kx, st));
+        ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 1 : 2 * bpe));
+        KB_TRY(launch_ln_mix(0, w.x, B, T, C, d.ln_out_w, d.ln_out_b, none, nullptr, nullptr,
+                             i8 ? nullptr : w.kx, st));
     }
     {
         ProfScope ps(PH_HEAD, st, 2.0 * R * (double)d.n_vocab * C);
-        if (logit_stats)
+        if (i8) {
+            const int8_t* hw = (const int8_t*)d.head;
+            if (logit_stats)
+                KB_TRY(launch_gemm_logits_i8(w.q_kx, C, w.s_kx, hw, C, d.head_scale, R,
+                                             d.vocab_pad, C, logits, d.vocab_pad, d.n_vocab,
+                                             logit_stats, d.vocab_pad / 32, st));
+            else
+                KB_TRY(launch_gemm_i8(w.q_kx, C, w.s_kx, hw, C, d.head_scale, R, d.vocab_pad, C,
+                                      KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));
+        } else if (logit_stats) {
             KB_TRY(launch_gemm_logits(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
                                       logits, d.vocab_pad, d.n_vocab, logit_stats,
                                       d.vocab_pad / 32, st));
-        else
-            KB_TRY(launch_gemm_f16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
+        } else {
+            KB_TRY(launch_gemm_tc(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
                                    KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));
+        }
     }
     return KB_OK;
 }

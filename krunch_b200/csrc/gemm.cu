@@ -4,19 +4,17 @@
 
 namespace kb {
 
-int launch_gemm_f16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
-                    int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
-                    const uint16_t* gate, cudaStream_t st) {
-    return launch_gemm_tc(A, lda, W, ldw, M, N, K, epi, out, ldo, resid, gate, st);
-}
-
 }  // namespace kb
 
-extern "C" int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw, int M,
-                       int N, int K, int epilogue, void* out, int64_t ldo, const uint16_t* resid,
-                       const uint16_t* gate, void* stream) {
+extern "C" int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
+                             int M, int N, int K, int epilogue, void* out, int64_t ldo,
+                             const uint16_t* resid, const uint16_t* gate, int tile_n,
+                             void* stream) {
     using namespace kb;
     if (!A || !W || !out || M < 0 || N <= 0 || K <= 0) return KB_ERR_ARG;
+    if (epilogue < KB_EPI_F32 || epilogue > KB_EPI_GATE_RESID) return KB_ERR_ARG;
+    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256)
+        return KB_ERR_ARG;
     if (dtype != KB_F16) return KB_ERR_UNSUPPORTED;
     if (N % 32 || K % 64) return KB_ERR_SHAPE;
     if ((epilogue == KB_EPI_RESID || epilogue == KB_EPI_GATE_RESID) && !resid) return KB_ERR_ARG;
@@ -24,9 +22,35 @@ extern "C" int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int
     if (!aligned16(A) || !aligned16(W) || (lda % 8) || (ldw % 8) || lda < K || ldw < K ||
         ldo < N || (ldo % 8) || !aligned16(out))
         return KB_ERR_ALIGN;
-    return launch_gemm_f16(reinterpret_cast<const uint16_t*>(A), lda,
-                           reinterpret_cast<const uint16_t*>(W), ldw, M, N, K, epilogue, out, ldo,
-                           resid, gate, as_stream(stream));
+    return launch_gemm_tc(reinterpret_cast<const uint16_t*>(A), lda,
+                          reinterpret_cast<const uint16_t*>(W), ldw, M, N, K, epilogue, out, ldo,
+                          resid, gate, as_stream(stream), tile_n);
+}
+
+extern "C" int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw, int M,
+                       int N, int K, int epilogue, void* out, int64_t ldo, const uint16_t* resid,
+                       const uint16_t* gate, void* stream) {
+    return kb_gemm_tiled(dtype, A, lda, W, ldw, M, N, K, epilogue, out, ldo, resid, gate, 0,
+                         stream);
+}
+
+extern "C" int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t* W,
+                          int64_t ldw, const uint16_t* w_scale, int M, int N, int K, int epilogue,
+                          void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
+                          int tile_n, void* stream) {
+    using namespace kb;
+    if (!A || !W || !out || !a_scale || !w_scale || M < 0 || N <= 0 || K <= 0) return KB_ERR_ARG;
+    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256)
+        return KB_ERR_ARG;
+    if (epilogue < KB_EPI_F32 || epilogue > KB_EPI_GATE_RESID) return KB_ERR_ARG;
+    if (N % 32 || K % 128) return KB_ERR_SHAPE;
+    if ((epilogue == KB_EPI_RESID || epilogue == KB_EPI_GATE_RESID) && !resid) return KB_ERR_ARG;
+    if (epilogue == KB_EPI_GATE_RESID && !gate) return KB_ERR_ARG;
+    if (!aligned16(A) || !aligned16(W) || !aligned16(w_scale) || (lda % 16) || (ldw % 16) ||
+        lda < K || ldw < K || ldo < N || (ldo % 8) || !aligned16(out))
+        return KB_ERR_ALIGN;
+    return launch_gemm_i8(A, lda, a_scale, W, ldw, w_scale, M, N, K, epilogue, out, ldo, resid,
+                          gate, as_stream(stream), tile_n);
 }
 
 extern "C" int kb_device_error_status(int reset) {

@@ -28,20 +28,48 @@
 
 namespace kb {
 
-constexpr int TC_BM = 128, TC_BN = 256, TC_BK = 64, TC_STAGES = 4, TC_NT = 576;
+constexpr int TC_BM = 128, TC_BK = 64, TC_NT = 576;
 constexpr int TC_EPI_WARPS = 16;
-constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;          // 16 KB
-constexpr uint32_t TC_B_BYTES = TC_BN * TC_BK * 2;          // 32 KB
-constexpr uint32_t TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;  // 48 KB
-constexpr uint32_t TC_TMEM_COLS = 2 * TC_BN;                // two accumulators
-constexpr size_t TC_SMEM = (size_t)TC_STAGES * TC_STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
-constexpr uint32_t TC_IDESC = tc::idesc_f16(TC_BM, TC_BN, false);
+constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
+
+// Tile width BN in {256, 128, 64, 32}: 256 for large M; narrower tiles give
+// a small-M launch (the decoder's B rows) more CTAs.  The K walk of an output
+// element is the same for every BN.
+enum { TC_F16 = 0, TC_I8 = 1 };
+
+template <int BN, int KIND>
+struct TcCfg {
+    static_assert(BN == 256 || BN == 128 || BN == 64 || BN == 32, "tile width");
+    // a K block is one 128-byte swizzle row: 64 fp16 or 128 int8 elements
+    static constexpr int KEL = KIND == TC_I8 ? 128 : 64;
+    static constexpr uint32_t B_BYTES = BN * 128;
+    static constexpr uint32_t STAGE_BYTES = TC_A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
+    static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+    static constexpr uint32_t IDESC =
+        KIND == TC_I8 ? tc::idesc_i8(TC_BM, BN) : tc::idesc_f16(TC_BM, BN, false);
+};
+
+// Launch parameters of one GEMM (a __grid_constant__ kernel argument).
+struct TcArgs {
+    int M, N, K;
+    void* out;
+    int64_t ldo;
+    const uint16_t* resid;
+    const uint16_t* gate;
+    int V;                    // head: valid vocabulary columns
+    float2* stats;            // head: subtile partials
+    int stats_stride;
+    const float* a_scale;     // int8: dequantisation factor per row of A
+    const uint16_t* w_scale;  // int8: fp16 dequantisation factor per row of W
+};
 
 __device__ int g_tc_error = 0;
 
 struct TcBars {
-    uint64_t full[TC_STAGES];
-    uint64_t empty[TC_STAGES];
+    uint64_t full[8];
+    uint64_t empty[8];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint32_t tmem_base;
@@ -62,12 +90,13 @@ __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 // changes fastest, so the CTAs running at the same time share a few weight
 // tiles (read from L2) and a few activation row blocks.
 constexpr int TC_GROUP_M = 16;
+template <int BN>
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m0, int& n0) {
     const int per_group = TC_GROUP_M * num_n;
     const int g = t / per_group, r = t - g * per_group;
     const int gm = min(TC_GROUP_M, num_m - g * TC_GROUP_M);
     m0 = (g * TC_GROUP_M + r % gm) * TC_BM;
-    n0 = (r / gm) * TC_BN;
+    n0 = (r / gm) * BN;
 }
 
 // Epilogue on 32 consecutive columns [c0, c0+32) of row r.
@@ -130,21 +159,47 @@ __device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* ou
     }
 }
 
-template <int EPI>
+// int8 accumulators of 32 columns -> fp32 values in place:
+// y = (float(acc) * a_scale[row]) * float(w_scale[col]), rounded at each step.
+__device__ __forceinline__ void dequant32(uint32_t (&v)[32], float sa, const uint16_t* ws) {
+    const uint4* w4 = reinterpret_cast<const uint4*>(ws);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 q = __ldg(w4 + j);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const float2 sw = __half22float2(*reinterpret_cast<const __half2*>(&qw[h]));
+            const int c = 8 * j + 2 * h;
+            v[c] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int)v[c]), sa), sw.x));
+            v[c + 1] =
+                __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int)v[c + 1]), sa), sw.y));
+        }
+    }
+}
+
+template <int EPI, int BN, int KIND>
 __global__ void __launch_bounds__(TC_NT, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              int M, int N, int K, void* out, int64_t ldo, const uint16_t* resid,
-              const uint16_t* gate, int V, float2* stats, int stats_stride) {
+              const __grid_constant__ TcArgs args) {
+    using Cfg = TcCfg<BN, KIND>;
+    const int M = args.M, N = args.N, K = args.K;
+    void* const out = args.out;
+    const int64_t ldo = args.ldo;
+    const int V = args.V, stats_stride = args.stats_stride;
+    float2* const stats = args.stats;
+    constexpr int TC_STAGES = Cfg::STAGES;
+    constexpr uint32_t TC_STAGE_BYTES = Cfg::STAGE_BYTES;
     extern __shared__ unsigned char tc_smem_raw[];
     const uint32_t raw = tc::smem_addr(tc_smem_raw);
     unsigned char* smem = tc_smem_raw + (((raw + 1023u) & ~1023u) - raw);
     TcBars* bars = reinterpret_cast<TcBars*>(smem + TC_STAGES * TC_STAGE_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int num_n = (N + TC_BN - 1) / TC_BN;
+    const int num_n = (N + BN - 1) / BN;
     const int num_m = (M + TC_BM - 1) / TC_BM;
     const int tiles = num_m * num_n;
-    const int KB = K / TC_BK;
+    const int KB = K / Cfg::KEL;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TC_STAGES; ++s) {
@@ -162,7 +217,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
         tc::prefetch_tmap(&mapA);
         tc::prefetch_tmap(&mapB);
     }
-    if (warp == 1) tc::tmem_alloc(&bars->tmem_base, TC_TMEM_COLS);
+    if (warp == 1) tc::tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -176,7 +231,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
             uint32_t issued = 0, issued_parity = 0;  // per-stage bit masks
             for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x) {
                 int m0, n0;
-                tile_coords(t, num_m, num_n, m0, n0);
+                tile_coords<BN>(t, num_m, num_n, m0, n0);
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1u)) {
                         tc_fail(bars, 1);
@@ -184,8 +239,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     }
                     unsigned char* sa = smem + stage * TC_STAGE_BYTES;
                     tc::mbar_expect_tx(&bars->full[stage], TC_STAGE_BYTES);
-                    tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * TC_BK, m0);
-                    tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * TC_BK, n0);
+                    tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * Cfg::KEL, m0);
+                    tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * Cfg::KEL, n0);
                     issued |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == TC_STAGES) {
@@ -213,7 +268,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     break;
                 }
                 tc::fence_after_sync();
-                const uint32_t d = tmem + (uint32_t)(a * TC_BN);
+                const uint32_t d = tmem + (uint32_t)(a * BN);
                 bool ok = true;
                 for (int kb = 0; kb < KB; ++kb) {
                     if (!tc::mbar_wait(&bars->full[stage], phase)) {
@@ -225,9 +280,14 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     const uint32_t sa = tc::smem_addr(smem + stage * TC_STAGE_BYTES);
                     const uint32_t sb = sa + TC_A_BYTES;
 #pragma unroll
-                    for (int j = 0; j < TC_BK / 16; ++j)
-                        tc::mma_f16(d, tc::sdesc_k128(sa + 32u * j), tc::sdesc_k128(sb + 32u * j),
-                                    TC_IDESC, (kb | j) != 0);
+                    for (int j = 0; j < 4; ++j) {  // 32 bytes of K per MMA
+                        if (KIND == TC_I8)
+                            tc::mma_i8(d, tc::sdesc_k128(sa + 32u * j),
+                                       tc::sdesc_k128(sb + 32u * j), Cfg::IDESC, (kb | j) != 0);
+                        else
+                            tc::mma_f16(d, tc::sdesc_k128(sa + 32u * j),
+                                        tc::sdesc_k128(sb + 32u * j), Cfg::IDESC, (kb | j) != 0);
+                    }
                     tc::mma_commit(&bars->empty[stage]);
                     if (++stage == TC_STAGES) {
                         stage = 0;
@@ -241,30 +301,36 @@ __global__ void __launch_bounds__(TC_NT, 1)
     } else {
         // ---------------- epilogue (warps 2..17) ----------------
         const int q = warp & 3;          // TMEM lane quadrant this warp may access
-        const int g = (warp - 2) >> 2;   // 64-column quarter of the tile
+        const int g = (warp - 2) >> 2;   // quarter of the tile's columns
         int i = 0;
         for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
             const int a = i & 1;
             const uint32_t use = (uint32_t)(i >> 1);
             int m0, n0;
-                tile_coords(t, num_m, num_n, m0, n0);
+            tile_coords<BN>(t, num_m, num_n, m0, n0);
             if (!tc::mbar_wait(&bars->tfull[a], use & 1u)) {
                 tc_fail(bars, 4);
                 break;
             }
             tc::fence_after_sync();
             const int64_t row = m0 + q * 32 + lane;
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * TC_BN);
+            const float sa = (KIND == TC_I8 && row < M) ? args.a_scale[row] : 0.0f;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+            // 32-column chunks [c_lo, c_hi) of this warp
+            constexpr int NCH = BN / 32;
+            const int c_lo = NCH >= 4 ? g * (NCH / 4) : g;
+            const int c_hi = NCH >= 4 ? c_lo + NCH / 4 : (g < NCH ? g + 1 : g);
             if (EPI == KB_EPI_LOGITS_STATS) {
                 // one pass per 32-column subtile: max of the fp16-rounded
                 // logits (columns < V), e = fp16(e^(x - m)), left-to-right sum
 #pragma unroll 1
-                for (int c = 2 * g; c < 2 * g + 2; ++c) {
+                for (int c = c_lo; c < c_hi; ++c) {
                     const int col0 = n0 + c * 32;
                     if (col0 >= N) break;
                     uint32_t v[32];
                     tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
                     tc::tmem_ld_wait();
+                    if (KIND == TC_I8) dequant32(v, sa, args.w_scale + col0);
                     float xr[32];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
@@ -317,13 +383,14 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 }
             } else {
 #pragma unroll 1
-                for (int c = 2 * g; c < 2 * g + 2; ++c) {
+                for (int c = c_lo; c < c_hi; ++c) {
                     const int col0 = n0 + c * 32;
                     if (col0 >= N) break;
                     uint32_t v[32];
                     tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
                     tc::tmem_ld_wait();
-                    if (row < M) tc_epi_store<EPI>(v, out, ldo, resid, gate, row, col0);
+                    if (KIND == TC_I8) dequant32(v, sa, args.w_scale + col0);
+                    if (row < M) tc_epi_store<EPI>(v, out, ldo, args.resid, args.gate, row, col0);
                 }
             }
             tc::fence_before_sync();
@@ -336,7 +403,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
     __syncthreads();
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, TC_TMEM_COLS);
+        tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
 }
 
@@ -358,18 +425,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// Row-major [rows, cols] fp16 with row stride ld (elements), boxed
-// box_rows x 64 with the 128-byte swizzle; out-of-range rows read as zero.
-bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows) {
+// Row-major [rows, cols] fp16 (elem 2) or int8 (elem 1) with row stride ld
+// elements, boxed box_rows x 128 bytes with the 128-byte swizzle; out-of-range
+// rows read as zero.
+bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld, int box_rows,
+              int elem) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * elem};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / elem), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return fn(map, elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+              const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int sm_count() {
@@ -385,53 +455,107 @@ int sm_count() {
     return cache[dev];
 }
 
-template <int EPI>
-int launch_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N, int K,
-              void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
-              cudaStream_t st, int V = 0, float2* stats = nullptr, int stats_stride = 0) {
+template <int EPI, int BN, int KIND>
+int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs& args,
+                 cudaStream_t st) {
+    using Cfg = TcCfg<BN, KIND>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)TC_SMEM);
+        attr_err = cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM);
     });
     if (attr_err != cudaSuccess) {
         set_cuda_error(attr_err);
         return KB_ERR_CUDA;
     }
-    CUtensorMap ma, mb;
-    if (!make_map(&ma, A, M, K, lda, TC_BM) || !make_map(&mb, W, N, K, ldw, TC_BN))
+    CUtensorMap mb;
+    if (!make_map(&mb, W, args.N, args.K, ldw, BN, KIND == TC_I8 ? 1 : 2))
         return KB_ERR_UNSUPPORTED;
-    const int tiles = ((M + TC_BM - 1) / TC_BM) * ((N + TC_BN - 1) / TC_BN);
+    const int tiles = ((args.M + TC_BM - 1) / TC_BM) * ((args.N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    k_gemm_tc<EPI><<<grid, TC_NT, TC_SMEM, st>>>(ma, mb, M, N, K, out, ldo, resid, gate, V, stats,
-                                                  stats_stride);
+    k_gemm_tc<EPI, BN, KIND><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, args);
     return launch_status();
+}
+
+// Tile width for a launch: the widest whose tile count fills the SMs, else
+// the narrowest.  Every width gives the same bits (one K walk per element).
+int pick_bn(int M, int N) {
+    const int mt = (M + TC_BM - 1) / TC_BM, sms = sm_count();
+    for (int bn = 256; bn > 32; bn >>= 1)
+        if (mt * ((N + bn - 1) / bn) >= sms) return bn;
+    return 32;
+}
+
+template <int EPI, int KIND>
+int launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, const TcArgs& args,
+              cudaStream_t st, int bn) {
+    CUtensorMap ma;
+    if (!make_map(&ma, A, args.M, args.K, lda, TC_BM, KIND == TC_I8 ? 1 : 2))
+        return KB_ERR_UNSUPPORTED;
+    if (bn == 0) bn = pick_bn(args.M, args.N);
+    switch (bn) {
+        case 256: return launch_tc_bn<EPI, 256, KIND>(ma, W, ldw, args, st);
+        case 128: return launch_tc_bn<EPI, 128, KIND>(ma, W, ldw, args, st);
+        case 64: return launch_tc_bn<EPI, 64, KIND>(ma, W, ldw, args, st);
+        case 32: return launch_tc_bn<EPI, 32, KIND>(ma, W, ldw, args, st);
+        default: return KB_ERR_ARG;
+    }
+}
+
+template <int KIND>
+int launch_epi(const void* A, int64_t lda, const void* W, int64_t ldw, int epi,
+               const TcArgs& args, cudaStream_t st, int bn) {
+    switch (epi) {
+        case KB_EPI_F32: return launch_tc<KB_EPI_F32, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_F16: return launch_tc<KB_EPI_F16, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_SIGMOID: return launch_tc<KB_EPI_SIGMOID, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_RELU_SQ: return launch_tc<KB_EPI_RELU_SQ, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_RESID: return launch_tc<KB_EPI_RESID, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_LOGITS_STATS: return launch_tc<KB_EPI_LOGITS_STATS, KIND>(A, lda, W, ldw, args, st, bn);
+        default: return KB_ERR_ARG;
+    }
 }
 
 }  // namespace
 
 int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M, int N,
                    int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
-                   const uint16_t* gate, cudaStream_t st) {
+                   const uint16_t* gate, cudaStream_t st, int bn) {
     if (M == 0) return KB_OK;
-    switch (epi) {
-        case KB_EPI_F32: return launch_tc<KB_EPI_F32>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        case KB_EPI_F16: return launch_tc<KB_EPI_F16>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        case KB_EPI_SIGMOID: return launch_tc<KB_EPI_SIGMOID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        case KB_EPI_RELU_SQ: return launch_tc<KB_EPI_RELU_SQ>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        case KB_EPI_RESID: return launch_tc<KB_EPI_RESID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID>(A, lda, W, ldw, M, N, K, out, ldo, resid, gate, st);
-        default: return KB_ERR_ARG;
-    }
+    if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, nullptr, nullptr};
+    return launch_epi<TC_F16>(A, lda, W, ldw, epi, args, st, bn);
+}
+
+int launch_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t* W,
+                   int64_t ldw, const uint16_t* w_scale, int M, int N, int K, int epi, void* out,
+                   int64_t ldo, const uint16_t* resid, const uint16_t* gate, cudaStream_t st,
+                   int bn) {
+    if (M == 0) return KB_OK;
+    if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, a_scale, w_scale};
+    return launch_epi<TC_I8>(A, lda, W, ldw, epi, args, st, bn);
 }
 
 int launch_gemm_logits(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M,
                        int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
                        int stats_stride, cudaStream_t st) {
     if (M == 0) return KB_OK;
-    return launch_tc<KB_EPI_LOGITS_STATS>(A, lda, W, ldw, M, N, K, out, ldo, nullptr, nullptr, st,
-                                          V, reinterpret_cast<float2*>(stats), stats_stride);
+    const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
+                      stats_stride, nullptr, nullptr};
+    return launch_epi<TC_F16>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
+}
+
+int launch_gemm_logits_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t* W,
+                          int64_t ldw, const uint16_t* w_scale, int M, int N, int K,
+                          uint16_t* out, int64_t ldo, int V, float* stats, int stats_stride,
+                          cudaStream_t st) {
+    if (M == 0) return KB_OK;
+    const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
+                      stats_stride, a_scale, w_scale};
+    return launch_epi<TC_I8>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
 }
 
 int read_tc_error(int reset) {

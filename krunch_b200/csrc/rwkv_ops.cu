@@ -7,6 +7,7 @@
 // single-row steps.  That is what lets the stepped decoder reproduce the
 // packed encoder's logits bit for bit.
 #include "kb_common.cuh"
+#include "quant.cuh"
 #include "rwkv_ops.cuh"
 
 namespace kb {
@@ -113,6 +114,34 @@ __device__ __forceinline__ void store_row_f16(uint16_t* __restrict__ dst, int la
     }
 }
 
+// Row quantised to int8 (quant.cuh) from the fp16 rounding of v; lane 0
+// writes the row's dequantisation factor to *qs.
+template <int EPL>
+__device__ __forceinline__ void store_row_q(int8_t* __restrict__ dst, float* qs, int lane,
+                                            const float (&v)[EPL]) {
+    float a[EPL], m = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) {
+        a[e] = __half2float(__float2half_rn(v[e]));
+        m = fmaxf(m, fabsf(a[e]));
+    }
+    const float amax = warp_max(m);
+    const float inv = q_inv(amax);
+    if (RowIdx<EPL>::VEC) {
+#pragma unroll
+        for (int j = 0; j < EPL / 8; ++j) {
+            const float* c = a + 8 * j;
+            reinterpret_cast<uint2*>(dst)[j * 32 + lane] =
+                make_uint2(pack4(q8(c[0], inv), q8(c[1], inv), q8(c[2], inv), q8(c[3], inv)),
+                           pack4(q8(c[4], inv), q8(c[5], inv), q8(c[6], inv), q8(c[7], inv)));
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e * 32 + lane] = (int8_t)q8(a[e], inv);
+    }
+    if (lane == 0) *qs = q_factor(amax);
+}
+
 // LN + token-shift mix, one warp per row, every row independent:
 //   prev(t) = state_in[b] for t == 0, else LN(x[t-1]) recomputed by this warp
 //   mix_j   = xx * m_j + prev * (1 - m_j)   (rwkv4_step_ref.py:59-61)
@@ -147,6 +176,7 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
     }
     ln_warp<EPL>(v, C, lane, lw, lb, cur);
     if (xx_out) store_row_f16<EPL>(xx_out + row * C, lane, cur);
+    if (NMIX == 0 && ma.q[0]) store_row_q<EPL>(ma.q[0] + row * C, ma.qs[0] + row, lane, cur);
 #pragma unroll
     for (int m = 0; m < NMIX; ++m) {
         float mk[EPL];
@@ -154,7 +184,10 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
 #pragma unroll
         for (int e = 0; e < EPL; ++e)
             mk[e] = __fmaf_rn(cur[e], mk[e], __fmul_rn(prev[e], __fsub_rn(1.0f, mk[e])));
-        store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
+        if (ma.q[m])
+            store_row_q<EPL>(ma.q[m] + row * C, ma.qs[m] + row, lane, mk);
+        else
+            store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
     }
     if (t == T - 1 && state_out) {
 #pragma unroll
@@ -296,6 +329,73 @@ int launch_embed(const int32_t* tok, int64_t rows, int V, int C, const uint16_t*
     return launch_status();
 }
 
+// Row-wise int8 quantisation of fp16 [R, K] (K % 8 == 0), one warp per row:
+// the (r*y) and relu(k)^2 operands of the w8a8 model.
+__global__ void __launch_bounds__(256) k_quant_rows(const uint16_t* __restrict__ x, int R, int K,
+                                                    int8_t* __restrict__ q,
+                                                    float* __restrict__ qs) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= R) return;
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * K);
+    const int n8 = K / 8;
+    float m = 0.0f;
+    for (int i = lane; i < n8; i += 32) {
+        const uint4 u = __ldg(src + i);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(h[k]);
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+    const float amax = warp_max(m);
+    const float inv = q_inv(amax);
+    uint2* dst = reinterpret_cast<uint2*>(q + row * K);
+    for (int i = lane; i < n8; i += 32) {
+        const uint4 u = __ldg(src + i);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+        float f[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 t = __half22float2(h[k]);
+            f[2 * k] = t.x;
+            f[2 * k + 1] = t.y;
+        }
+        dst[i] = make_uint2(pack4(q8(f[0], inv), q8(f[1], inv), q8(f[2], inv), q8(f[3], inv)),
+                            pack4(q8(f[4], inv), q8(f[5], inv), q8(f[6], inv), q8(f[7], inv)));
+    }
+    if (lane == 0) qs[row] = q_factor(amax);
+}
+
+// Per-output-channel weight quantisation of fp16 [N, K], one warp per row:
+// s = fp16(amax / 127), q = clamp(rint(w / s), -127, 127).
+__global__ void __launch_bounds__(256) k_quant_weight(const uint16_t* __restrict__ w, int N, int K,
+                                                      int8_t* __restrict__ q,
+                                                      uint16_t* __restrict__ scale) {
+    const int lane = threadIdx.x & 31;
+    const int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const uint16_t* src = w + n * K;
+    float m = 0.0f;
+    for (int i = lane; i < K; i += 32) m = fmaxf(m, fabsf(h2f(src[i])));
+    const float amax = warp_max(m);
+    const uint16_t sh = f2h(__fdiv_rn(amax, 127.0f));
+    const float s = h2f(sh);
+    for (int i = lane; i < K; i += 32) {
+        const float r = s > 0.0f ? rintf(__fdiv_rn(h2f(src[i]), s)) : 0.0f;
+        q[n * K + i] = (int8_t)fminf(fmaxf(r, -127.0f), 127.0f);
+    }
+    if (lane == 0) scale[n] = sh;
+}
+
+int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, cudaStream_t st) {
+    if (R == 0) return KB_OK;
+    if (K % 8) return KB_ERR_SHAPE;
+    k_quant_rows<<<(R + 7) / 8, 256, 0, st>>>(x, R, K, q, scale);
+    return launch_status();
+}
+
 template <int NMIX>
 static int ln_mix_epl(int epl, int blocks, cudaStream_t st, const uint16_t* x, int B, int T, int C,
                       const float* lw, const float* lb, const MixArgs& ma, const float* state_in,
@@ -353,6 +453,20 @@ int launch_state_init(float* st, int L, int B, int C, cudaStream_t s) {
 }
 
 }  // namespace kb
+
+extern "C" int kb_quantize_weight(const uint16_t* w, int N, int K, int8_t* q, uint16_t* scale,
+                                  void* stream) {
+    if (!w || !q || !scale || N <= 0 || K <= 0) return KB_ERR_ARG;
+    kb::k_quant_weight<<<(N + 7) / 8, 256, 0, kb::as_stream(stream)>>>(w, N, K, q, scale);
+    return kb::launch_status();
+}
+
+extern "C" int kb_quantize_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale,
+                                void* stream) {
+    if (!x || !q || !scale || R < 0 || K <= 0) return KB_ERR_ARG;
+    if (!kb::aligned16(x) || ((uintptr_t)q & 7u)) return KB_ERR_ALIGN;
+    return kb::launch_quant_rows(x, R, K, q, scale, kb::as_stream(stream));
+}
 
 extern "C" int kb_prepare_decay(const float* td, float* out, int n, void* stream) {
     if (!td || !out || n < 0) return KB_ERR_ARG;

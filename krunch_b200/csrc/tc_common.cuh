@@ -93,6 +93,17 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, one 128 x N x 32 step (kind::i8, s8 x s8
+// -> s32: exact integer accumulation).
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                      uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 // Arrive on `bar` once every previously issued MMA of this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile(
@@ -141,6 +152,13 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
     return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor of kind::i8: D s32 (bits 4-5 = 2), A and B signed
+// 8-bit (7-9, 10-12 = 1), both K-major, N >> 3 at 17-22, M >> 4 at 24-28.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
 }
 
 }  // namespace tc

@@ -4,6 +4,10 @@ Replaces krunch/cpp_path.py:init_weights / fresh_state (cpp_path.py:26-106).
 Weights arrive in the reference's ``model.w`` layout (matrices [in, out],
 time_decay as the raw log-decay of rwkv4_step_ref.py:89) and are stored on
 the device K-major ([out, in], fp16) for the GEMMs.
+
+``wdtype="i8"`` is the w8a8 model: every matrix (head included) quantised
+per output channel to int8 with fp16 factors (kb_quantize_weight), the GEMM
+inputs quantised per row at run time.
 """
 from __future__ import annotations
 
@@ -41,8 +45,8 @@ class RWKVModel:
     """Device-resident RWKV-4 with a kb_model handle."""
 
     def __init__(self, w: dict, device="cuda", wkv: str = "step_ref", wdtype: str = "f16"):
-        if wdtype != "f16":
-            raise NotImplementedError(f"weight dtype {wdtype!r} is not built yet")
+        if wdtype not in ("f16", "i8"):
+            raise ValueError(f"unknown weight dtype {wdtype!r}")
         if wkv not in ("step_ref", "production"):
             raise ValueError(f"unknown WKV convention {wkv!r}")
         self.device = torch.device(device)
@@ -60,13 +64,31 @@ class RWKVModel:
             self._keep.append(t)
             return t
 
-        def kmajor(a):  # [in, out] -> fp16 [out, in]
+        stream = N.stream_ptr(dev)
+        i8 = wdtype == "i8"
+
+        def quantize(t16):  # fp16 [N, K] -> (int8 [N, K], fp16 scales [N])
+            q = torch.empty(t16.shape, dtype=torch.int8, device=dev)
+            sc = torch.empty(t16.shape[0], dtype=torch.float16, device=dev)
+            N.call("kb_quantize_weight", t16.data_ptr(), t16.shape[0], t16.shape[1], q.data_ptr(),
+                   sc.data_ptr(), stream)
+            self._keep += [q, sc]
+            return q, sc
+
+        def kmajor(a):  # [in, out] -> fp16 [out, in]  (int8 + scales for i8)
             t = torch.as_tensor(np.asarray(a, dtype=np.float32)).to(dev)
             t = t.t().contiguous().to(torch.float16)
+            if i8:
+                return quantize(t)
             self._keep.append(t)
-            return t
+            return t, None
 
-        stream = N.stream_ptr(dev)
+        def mat(d, name, arr):
+            q, sc = kmajor(arr)
+            setattr(d, name + "w", q.data_ptr())
+            if sc is not None:
+                setattr(d, name + "s", sc.data_ptr())
+
         self.emb = torch.as_tensor(np.asarray(w["emb.weight"], np.float32)).to(dev).half().contiguous()
         self._keep.append(self.emb)
         layers = (N.LayerDesc * L)()
@@ -84,31 +106,36 @@ class RWKVModel:
             d.att_mix_r = f32(w[att + "time_mix_r"]).data_ptr()
             d.att_decay = decay.data_ptr()
             d.att_first = f32(w[att + "time_first"]).data_ptr()
-            d.att_kw = kmajor(w[att + "key.weight"]).data_ptr()
-            d.att_vw = kmajor(w[att + "value.weight"]).data_ptr()
-            d.att_rw = kmajor(w[att + "receptance.weight"]).data_ptr()
-            d.att_ow = kmajor(w[att + "output.weight"]).data_ptr()
+            mat(d, "att_k", w[att + "key.weight"])
+            mat(d, "att_v", w[att + "value.weight"])
+            mat(d, "att_r", w[att + "receptance.weight"])
+            mat(d, "att_o", w[att + "output.weight"])
             d.ffn_mix_k = f32(w[ffn + "time_mix_k"]).data_ptr()
             d.ffn_mix_r = f32(w[ffn + "time_mix_r"]).data_ptr()
-            d.ffn_kw = kmajor(w[ffn + "key.weight"]).data_ptr()
-            d.ffn_vw = kmajor(w[ffn + "value.weight"]).data_ptr()
-            d.ffn_rw = kmajor(w[ffn + "receptance.weight"]).data_ptr()
+            mat(d, "ffn_k", w[ffn + "key.weight"])
+            mat(d, "ffn_v", w[ffn + "value.weight"])
+            mat(d, "ffn_r", w[ffn + "receptance.weight"])
         Vp = self.spec.vocab_pad
         head = torch.zeros((Vp, Cm), dtype=torch.float16, device=dev)
         head[:V] = torch.as_tensor(np.asarray(w["head.weight"], np.float32)).to(dev).t().half()
+        self.head_scale = None
+        if i8:
+            head, self.head_scale = quantize(head)
+        else:
+            self._keep.append(head)
         self.head = head
-        self._keep.append(head)
         self._layers = layers
         desc = N.ModelDesc()
         desc.n_layer, desc.n_embd, desc.n_ffn, desc.n_vocab = L, Cm, F, V
         desc.vocab_pad = Vp
-        desc.wdtype = N.KB_F16
+        desc.wdtype = N.KB_I8 if i8 else N.KB_F16
         desc.wkv_convention = N.KB_WKV_STEP_REF if wkv == "step_ref" else N.KB_WKV_PRODUCTION
         desc.emb = self.emb.data_ptr()
         desc.ln_out_w = f32(w["ln_out.weight"]).data_ptr()
         desc.ln_out_b = f32(w["ln_out.bias"]).data_ptr()
         desc.head = head.data_ptr()
         desc.layers = layers
+        desc.head_scale = None if self.head_scale is None else self.head_scale.data_ptr()
         handle = C.c_void_p()
         N.call("kb_model_create", C.byref(desc), C.byref(handle))
         self.handle = handle

@@ -53,9 +53,60 @@ def _mm(x: np.ndarray, W: np.ndarray) -> np.ndarray:
     return (x.reshape(B * T, C) @ W).reshape(B, T, W.shape[1])
 
 
+# ---- w8a8 (the build's KB_I8 model; the reference has no w8a8 path) --------
+
+def quantize_weight(W: np.ndarray):
+    """[in, out] matrix -> int8 [out, in] and fp16 factor per output channel:
+    s = fp16(max|w| / 127), q = clamp(rint(w / s), -127, 127), from the fp16
+    weights the device holds."""
+    w16 = np.asarray(W, np.float32).T.astype(np.float16).astype(np.float32)
+    amax = np.abs(w16).max(axis=1)
+    s = (amax / np.float32(127)).astype(np.float32).astype(np.float16)
+    sf = s.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(sf[:, None] > 0, np.rint(w16 / sf[:, None]), 0)
+    return np.clip(q, -127, 127).astype(np.int8), s
+
+
+def quantize_rows(x: np.ndarray):
+    """fp32 rows [R, K] -> int8 [R, K] and fp32 factor per row, from the fp16
+    rounding of x: q = clamp(rint(a * (127 / amax)), -127, 127), factor amax / 127."""
+    a = np.asarray(x, np.float32).astype(np.float16).astype(np.float32)
+    amax = np.abs(a).max(axis=1)
+    inv = np.where(amax > 0, np.float32(127) / np.where(amax > 0, amax, 1), 0).astype(np.float32)
+    q = np.clip(np.rint(a * inv[:, None]), -127, 127).astype(np.int8)
+    return q, (amax / np.float32(127)).astype(np.float32)
+
+
+def _mm8(x: np.ndarray, Wq) -> np.ndarray:
+    """w8a8 product: exact integer accumulation, then (acc * sa) * sw."""
+    q, s = Wq
+    B, T, C = x.shape
+    qa, sa = quantize_rows(x.reshape(B * T, C))
+    acc = qa.astype(np.int64) @ q.astype(np.int64).T
+    y = (acc.astype(np.float32) * sa[:, None]) * s.astype(np.float32)[None, :]
+    return y.reshape(B, T, q.shape[0])
+
+
 def forward(w: dict, tokens: np.ndarray, state: list[np.ndarray] | None = None,
-            wkv: str = "step_ref") -> tuple[np.ndarray, list[np.ndarray]]:
-    """tokens int [B, T] -> (logits fp32 [B, T, V], new state)."""
+            wkv: str = "step_ref", wdtype: str = "f32") -> tuple[np.ndarray, list[np.ndarray]]:
+    """tokens int [B, T] -> (logits fp32 [B, T, V], new state).
+
+    wdtype "i8" runs the w8a8 model: every matrix product through _mm8, and
+    the activations the device keeps in fp16 (embedding, residual stream,
+    LayerNorm outputs, sigmoid gates) rounded to fp16 where the device rounds
+    them, so that the per-row quantisation sees the device's values."""
+    h = (lambda a: a.astype(np.float16).astype(np.float32)) if wdtype == "i8" else (lambda a: a)
+    if wdtype == "i8":
+        qcache = {}
+
+        def mm(x, name):
+            if name not in qcache:
+                qcache[name] = quantize_weight(w[name])
+            return _mm8(x, qcache[name])
+    else:
+        def mm(x, name):
+            return _mm(x, w[name])
     tok = np.asarray(tokens)
     if tok.ndim == 1:
         tok = tok[None]
@@ -63,19 +114,19 @@ def forward(w: dict, tokens: np.ndarray, state: list[np.ndarray] | None = None,
     if state is None:
         state = init_state(w, B)
     state = [s.copy() for s in state]
-    x = w["emb.weight"][tok].astype(np.float32)
+    x = h(w["emb.weight"][tok].astype(np.float32))
     for i in range(n_layer_of(w)):
         b, att, ffn = f"blocks.{i}.", f"blocks.{i}.att.", f"blocks.{i}.ffn."
         s = state[5 * i:5 * i + 5]
-        xx = layer_norm(x, w[b + "ln1.weight"], w[b + "ln1.bias"])
+        xx = h(layer_norm(x, w[b + "ln1.weight"], w[b + "ln1.bias"]))
         sx = _shift(xx, s[0])
         mk, mv, mr = (w[att + n].reshape(-1) for n in ("time_mix_k", "time_mix_v", "time_mix_r"))
         kx = xx * mk + sx * (1 - mk)
         vx = xx * mv + sx * (1 - mv)
         rx = xx * mr + sx * (1 - mr)
-        r = _sigmoid(_mm(rx, w[att + "receptance.weight"]))
-        k = _mm(kx, w[att + "key.weight"])
-        v = _mm(vx, w[att + "value.weight"])
+        r = h(_sigmoid(mm(rx, att + "receptance.weight")))
+        k = mm(kx, att + "key.weight")
+        v = mm(vx, att + "value.weight")
         u = w[att + "time_first"].reshape(-1)
         decay = np.exp(w[att + "time_decay"].reshape(-1)).astype(np.float32)
         aa, bb, pp = s[1], s[2], s[3]
@@ -97,21 +148,21 @@ def forward(w: dict, tokens: np.ndarray, state: list[np.ndarray] | None = None,
             aa = f1 * aa + f2 * vt
             bb = f1 * bb + f2
             pp = p2
-        x = x + _mm(r * y, w[att + "output.weight"])
+        x = h(x + mm(r * y, att + "output.weight"))
         state[5 * i + 0] = xx[:, -1].copy()
         state[5 * i + 1], state[5 * i + 2], state[5 * i + 3] = aa, bb, pp
 
-        xx2 = layer_norm(x, w[b + "ln2.weight"], w[b + "ln2.bias"])
+        xx2 = h(layer_norm(x, w[b + "ln2.weight"], w[b + "ln2.bias"]))
         sx2 = _shift(xx2, s[4])
         fk, fr = (w[ffn + n].reshape(-1) for n in ("time_mix_k", "time_mix_r"))
         kx2 = xx2 * fk + sx2 * (1 - fk)
         rx2 = xx2 * fr + sx2 * (1 - fr)
-        r2 = _sigmoid(_mm(rx2, w[ffn + "receptance.weight"]))
-        kk = np.maximum(_mm(kx2, w[ffn + "key.weight"]), 0) ** 2
-        x = x + r2 * _mm(kk, w[ffn + "value.weight"])
+        r2 = h(_sigmoid(mm(rx2, ffn + "receptance.weight")))
+        kk = np.maximum(mm(kx2, ffn + "key.weight"), 0) ** 2
+        x = h(x + r2 * mm(kk, ffn + "value.weight"))
         state[5 * i + 4] = xx2[:, -1].copy()
-    x = layer_norm(x, w["ln_out.weight"], w["ln_out.bias"])
-    return _mm(x, w["head.weight"]), state
+    x = h(layer_norm(x, w["ln_out.weight"], w["ln_out.bias"]))
+    return mm(x, "head.weight"), state
 
 
 def softmax(logits: np.ndarray) -> np.ndarray:

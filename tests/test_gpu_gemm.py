@@ -66,3 +66,31 @@ def test_m_invariance(torch):
         assert torch.equal(part, full[:M]), M
     rows = A[[5, 900, 3]].contiguous()
     assert torch.equal(_gemm(torch, rows, W, N.KB_EPI_F32), full[[5, 900, 3]])
+
+
+def _gemm_tiled(torch, A, W, epi, tile_n, resid=None, gate=None):
+    from krunch_b200 import _native as N
+    M, K = A.shape
+    Nn = W.shape[0]
+    dt = torch.float32 if epi == N.KB_EPI_F32 else torch.float16
+    out = resid.clone() if resid is not None else torch.empty((M, Nn), dtype=dt, device="cuda")
+    N.call("kb_gemm_tiled", N.KB_F16, A.data_ptr(), K, W.data_ptr(), K, M, Nn, K, epi,
+           out.data_ptr(), Nn, None if resid is None else out.data_ptr(),
+           None if gate is None else gate.data_ptr(), tile_n, N.stream_ptr())
+    return out
+
+
+@pytest.mark.parametrize("epi", range(6))
+@pytest.mark.parametrize("M,N,K", [(256, 768, 768), (33, 3072, 768), (300, 768, 3072)])
+def test_tile_width_invariance(torch, epi, M, N, K):
+    """Every output tile width gives the same bits (the decoder's small-M
+    launches use narrow tiles, the encoder's packed launches 256 wide)."""
+    g = torch.Generator(device="cuda").manual_seed(M + N + K + epi)
+    A = (torch.randn((M, K), device="cuda", generator=g) * 0.5).half()
+    W = (torch.randn((N, K), device="cuda", generator=g) * 0.05).half()
+    resid = torch.randn((M, N), device="cuda", generator=g).half()
+    gate = torch.rand((M, N), device="cuda", generator=g).half()
+    r, gt = (resid if epi >= 4 else None), (gate if epi == 5 else None)
+    want = _gemm_tiled(torch, A, W, epi, 256, r, gt)
+    for tn in (128, 64, 32, 0):
+        assert torch.equal(_gemm_tiled(torch, A, W, epi, tn, r, gt), want), tn

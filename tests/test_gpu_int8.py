@@ -1,0 +1,168 @@
+"""w8a8 int8 path (the KB_I8 model of BASELINE's decompress config): weight and
+activation quantisation bit-exact against the oracle, the kind::i8 GEMM
+bit-exact against exact integer arithmetic, tile-width / M invariance, the
+int8 model's logits against the oracle's w8a8 forward, and packed vs stepped
+bit identity.  The reference's own int8 GEMM is w8a16
+(krunch_ac/cuda/det_matmul_tc_uint8.cu:43-254); parity for w8a8 is against
+oracle/rwkv.py's restatement of this scheme."""
+import numpy as np
+import pytest
+
+from krunch_b200.synth import random_weights
+
+pytestmark = pytest.mark.gpu
+I8_MEAN_TOL = 2e-2
+I8_MAX_TOL = 0.15
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch as t
+    return t
+
+
+def test_quantize_weight_matches_oracle(torch):
+    from krunch_b200 import _native as N
+    from oracle import rwkv
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((384, 200)) * 0.02).astype(np.float32)  # [in, out]
+    W[:, 7] = 0.0  # an all-zero output channel
+    t = torch.from_numpy(W.T.astype(np.float16).copy()).cuda()
+    q = torch.empty((200, 384), dtype=torch.int8, device="cuda")
+    s = torch.empty(200, dtype=torch.float16, device="cuda")
+    N.call("kb_quantize_weight", t.data_ptr(), 200, 384, q.data_ptr(), s.data_ptr(), N.stream_ptr())
+    qo, so = rwkv.quantize_weight(W)
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy().view(np.uint16), so.view(np.uint16))
+
+
+@pytest.mark.parametrize("K", [128, 768, 3072])
+def test_quantize_rows_matches_oracle(torch, K):
+    from krunch_b200 import _native as N
+    from oracle import rwkv
+    rng = np.random.default_rng(K)
+    x = (rng.standard_normal((37, K)) * rng.uniform(0.01, 30, (37, 1))).astype(np.float16)
+    x[3] = 0
+    t = torch.from_numpy(x).cuda()
+    q = torch.empty((37, K), dtype=torch.int8, device="cuda")
+    s = torch.empty(37, dtype=torch.float32, device="cuda")
+    N.call("kb_quantize_rows", t.data_ptr(), 37, K, q.data_ptr(), s.data_ptr(), N.stream_ptr())
+    qo, so = rwkv.quantize_rows(x.astype(np.float32))
+    assert np.array_equal(q.cpu().numpy(), qo)
+    assert np.array_equal(s.cpu().numpy(), so)
+
+
+def _gemm8(torch, qa, sa, qw, sw, epi, tile_n=0, resid=None, gate=None):
+    from krunch_b200 import _native as N
+    M, K = qa.shape
+    Nn = qw.shape[0]
+    dt = torch.float32 if epi == N.KB_EPI_F32 else torch.float16
+    out = resid.clone() if resid is not None else torch.empty((M, Nn), dtype=dt, device="cuda")
+    N.call("kb_gemm_i8", qa.data_ptr(), K, sa.data_ptr(), qw.data_ptr(), K, sw.data_ptr(), M, Nn, K,
+           epi, out.data_ptr(), Nn, None if resid is None else out.data_ptr(),
+           None if gate is None else gate.data_ptr(), tile_n, N.stream_ptr())
+    return out
+
+
+def _operands(torch, M, Nn, K, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    qa = torch.randint(-127, 128, (M, K), device="cuda", generator=g, dtype=torch.int8)
+    qw = torch.randint(-127, 128, (Nn, K), device="cuda", generator=g, dtype=torch.int8)
+    sa = torch.rand(M, device="cuda", generator=g) * 1e-3
+    sw = (torch.rand(Nn, device="cuda", generator=g) * 1e-3).half()
+    return qa, sa, qw, sw
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 128), (77, 256, 384), (300, 768, 768), (129, 3072, 768),
+                                   (256, 768, 3072)])
+def test_gemm_i8_exact(torch, M, N, K):
+    """F32 epilogue: fp32((float(acc) * sa) * sw) with acc the exact integer
+    dot product — bit-exact against numpy."""
+    from krunch_b200 import _native as N_
+    qa, sa, qw, sw = _operands(torch, M, N, K, M + N + K)
+    out = _gemm8(torch, qa, sa, qw, sw, N_.KB_EPI_F32).cpu().numpy()
+    acc = qa.cpu().numpy().astype(np.int64) @ qw.cpu().numpy().astype(np.int64).T
+    want = (acc.astype(np.float32) * sa.cpu().numpy()[:, None]) * \
+        sw.cpu().numpy().astype(np.float32)[None, :]
+    assert np.array_equal(out, want.astype(np.float32))
+
+
+@pytest.mark.parametrize("epi", range(6))
+def test_gemm_i8_epilogues_and_tile_invariance(torch, epi):
+    from krunch_b200 import _native as N
+    M, Nn, K = 200, 768, 768
+    qa, sa, qw, sw = _operands(torch, M, Nn, K, 100 + epi)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    resid = torch.randn((M, Nn), device="cuda", generator=g).half()
+    gate = torch.rand((M, Nn), device="cuda", generator=g).half()
+    r, gt = (resid if epi >= 4 else None), (gate if epi == 5 else None)
+    y = _gemm8(torch, qa, sa, qw, sw, N.KB_EPI_F32)
+    ref = {0: y, 1: y, 2: torch.sigmoid(y), 3: torch.relu(y) ** 2,
+           4: resid.float() + y, 5: resid.float() + gate.float() * y}[epi]
+    want = _gemm8(torch, qa, sa, qw, sw, epi, 256, r, gt)
+    tol = 0 if epi == 0 else 2e-2
+    assert (want.float() - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
+    for tn in (128, 64, 32, 0):
+        assert torch.equal(_gemm8(torch, qa, sa, qw, sw, epi, tn, r, gt), want), tn
+    # M invariance: a subset of rows alone gives the same bits
+    sub = _gemm8(torch, qa[:33].contiguous(), sa[:33].contiguous(), qw, sw, epi, 0,
+                 None if r is None else r[:33].contiguous(), None if gt is None else gt[:33].contiguous())
+    assert torch.equal(sub, want[:33])
+
+
+def _run(torch, m, tokens, state=None):
+    tok = torch.from_numpy(np.ascontiguousarray(tokens, dtype=np.int32)).cuda()
+    B, T = tok.shape
+    st = m.new_state(B) if state is None else state
+    lg = m.new_logits(B, T)
+    m.forward_window(tok, st, m.new_workspace(B, T), lg)
+    return lg[:, :m.spec.n_vocab].float().view(B, T, -1).cpu().numpy(), st
+
+
+@pytest.mark.parametrize("shape", [(2, 128, 512, 300), (12, 768, 3072, 50277)])
+def test_i8_model_vs_oracle(torch, shape):
+    from krunch_b200.model import RWKVModel
+    from oracle import rwkv
+    w = random_weights(*shape, seed=3)
+    m = RWKVModel(w, wdtype="i8")
+    tok = np.random.default_rng(4).integers(0, shape[3], (2, 5))
+    lg, _ = _run(torch, m, tok)
+    ref, _ = rwkv.forward(w, tok, wdtype="i8")
+    d = np.abs(lg - ref)
+    # Per-row int8 quantisation turns last-bit differences (the device's exp,
+    # LayerNorm sum order) into +-1 flips of quantised values: in the oracle
+    # alone, a 1e-6 relative perturbation of every GEMM output moves the
+    # 169M logits by 0.088 max / 0.012 mean.  The bar is that noise level.
+    assert d.mean() <= I8_MEAN_TOL and d.max() <= I8_MAX_TOL, (d.mean(), d.max())
+    # and the w8a8 model stays near the fp32 model
+    ref32, _ = rwkv.forward(w, tok)
+    assert np.abs(lg - ref32).mean() <= 0.05
+
+
+def test_i8_packed_equals_stepped_bitwise(torch):
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=5), wdtype="i8")
+    tok = np.random.default_rng(1).integers(0, 300, (3, 20))
+    packed, st_p = _run(torch, m, tok)
+    st = m.new_state(3)
+    steps = []
+    for t in range(20):
+        lg, st = _run(torch, m, tok[:, t:t + 1], st)
+        steps.append(lg[:, 0])
+    assert np.array_equal(np.stack(steps, 1), packed)
+    assert torch.equal(st, st_p)
+    one, _ = _run(torch, m, tok[1:2])
+    assert np.array_equal(one[0], packed[1])
+
+
+def test_i8_codec_roundtrip(torch):
+    from krunch_b200.codec import Codec
+    from krunch_b200.model import RWKVModel
+    from krunch_b200.synth import zipf_tokens
+    m = RWKVModel(random_weights(12, 768, 3072, 50277, seed=0), wdtype="i8")
+    codec = Codec(m, cdf_bits=16)
+    seqs = list(zipf_tokens((6, 40), seed=9)) + [np.array([5], np.int32), np.zeros(0, np.int32)]
+    streams = codec.compress_tokens(seqs)
+    back = codec.decompress_tokens(streams, [len(s) for s in seqs])
+    for a, b in zip(seqs, back):
+        assert np.array_equal(a, b)
