@@ -291,6 +291,29 @@ int kb_forward_window(const kb_model* model, const int32_t* tokens, int B, int T
                       float* state, void* workspace, size_t workspace_bytes,
                       uint16_t* logits, float* logit_stats, void* stream);
 
+/* Fused stepped decode forward (T = 1) of a KB_I8 model: the whole layer
+ * stack in one persistent cooperative launch (one CTA per SM, grid barriers
+ * between phases, tcgen05 kind::i8 GEMM tiles with int8 weights staged
+ * through shared memory by TMA), then the head GEMM.  Same contract and the
+ * same bits as kb_forward_window(model, tokens, B, 1, ...): logits (or
+ * numerators + stats) and the state it advances.  Replaces the reference's
+ * fused single-token layers (krunch_ac/cuda/rwkv_step_v3.cu:83-480) and the
+ * launch chain of forward_stepped_batched (krunch/cpp_path.py:428-460).
+ * The workspace (kb_step_workspace_bytes) must stay the same buffer across
+ * calls to reuse the cached launch parameters; n_layer <= 24,
+ * n_embd in {128, 768, 2048}.  KB_ERR_UNSUPPORTED for fp16 models. */
+size_t kb_step_workspace_bytes(const kb_model* model, int B);
+int kb_step_forward(kb_model* model, const int32_t* tokens, int B, float* state,
+                    void* workspace, size_t workspace_bytes, uint16_t* logits,
+                    float* logit_stats, void* stream);
+/* Profiling aid: a device buffer of >= 512 u64 receives, for CTA 0 of each
+ * later kb_step_forward, %globaltimer at every grid barrier's entry (slot
+ * 2e) and exit (slot 2e+1); NULL turns it off. */
+int kb_step_set_trace(unsigned long long* trace);
+/* Device-side failure report of the fused step (bounded mbarrier and grid
+ * barrier waits): KB_OK or KB_ERR_TIMEOUT; reset != 0 clears it. */
+int kb_step_error_status(int reset);
+
 /* Allocation-free variant of kb_forward_window.  No counterpart in the
  * reference: it exists for hosts that cannot allocate device memory when they
  * run a forward, e.g. a decode loop being recorded into a CUDA graph (device

@@ -61,6 +61,10 @@ SIGNATURES = {
     "kb_decode_logits_step": (i32, [vp, i64, i32, i32, i32, vp, i64, vp, i64, vp, vp, vp, vp, vp, i64, vp]),
     "kb_device_error_status": (i32, [i32]),
     "kb_gemm": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, vp]),
+    "kb_step_workspace_bytes": (sz, [vp, i32]),
+    "kb_step_forward": (i32, [vp, vp, i32, vp, vp, sz, vp, vp, vp]),
+    "kb_step_error_status": (i32, [i32]),
+    "kb_step_set_trace": (i32, [vp]),
     "kb_gemm_i8": (i32, [vp, i64, vp, vp, i64, vp, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),
     "kb_quantize_weight": (i32, [vp, i32, i32, vp, vp, vp]),
     "kb_quantize_rows": (i32, [vp, i32, i32, vp, vp, vp]),
@@ -131,7 +135,7 @@ def call(name: str, *args) -> None:
     check(getattr(lib, name)(*args), name)
 
 
-PHASES = ("embed", "ln_mix", "gemm", "wkv", "head", "cdf", "encode", "decode")
+PHASES = ("embed", "ln_mix", "gemm", "wkv", "head", "cdf", "encode", "decode", "step")
 
 
 def profile_begin() -> None:

@@ -198,8 +198,10 @@ class CompressPlan:
 
     def launches_per_run(self) -> int:
         """Kernels of this library that run() launches."""
-        L = self.codec.model.spec.n_layer
-        per_window = 1 + 10 * L + 2 + 2   # embed, layers, ln_out+head, cdf+encode
+        m = self.codec.model
+        L = m.spec.n_layer
+        per_layer = 12 if m.spec.wdtype == "i8" else 10  # + 2 row quantisations
+        per_window = 1 + per_layer * L + 2 + 2   # embed, layers, ln_out+head, cdf+encode
         return 2 + self.windows * per_window + 1
 
     def fetch(self) -> list[bytes]:
@@ -240,7 +242,8 @@ class DecompressPlan:
         self.history = torch.zeros((B, max(self.Tmax, 1)), dtype=torch.int32, device=dev)
         self.cur = torch.zeros((B, 1), dtype=torch.int32, device=dev)
         self.state = m.new_state(B)
-        self.ws = m.new_workspace(B, 1)
+        self.fused = m.has_fused_step and N.env_flag("KRUNCH_FUSED_STEP", "1")
+        self.ws = m.new_step_workspace(B) if self.fused else m.new_workspace(B, 1)
         self.logits = m.new_logits(B, 1)
         self.stats = m.new_stats(B, 1)
         self.graph = None
@@ -257,7 +260,10 @@ class DecompressPlan:
 
     def _step(self) -> None:
         c, m = self.codec, self.codec.model
-        m.forward_window(self.cur, self.state, self.ws, self.logits, self.stats)
+        if self.fused:
+            m.step_forward(self.cur.view(-1), self.state, self.ws, self.logits, self.stats)
+        else:
+            m.forward_window(self.cur, self.state, self.ws, self.logits, self.stats)
         N.call("kb_decode_logits_step", self.logits.data_ptr(), m.spec.vocab_pad, self.B,
                m.spec.n_vocab, c.bits, self.stats.data_ptr(), m.stats_stride, self.in_d.data_ptr(),
                self.nbytes, self.offs_d.data_ptr(),
@@ -285,8 +291,11 @@ class DecompressPlan:
                 self._step()
 
     def launches_per_run(self) -> int:
-        L = self.codec.model.spec.n_layer
-        return 2 + self.Tmax * (1 + 10 * L + 2 + 1)
+        m = self.codec.model
+        if self.fused:
+            return 2 + self.Tmax * 3  # fused layers, head, decode
+        per_layer = 12 if m.spec.wdtype == "i8" else 10
+        return 2 + self.Tmax * (1 + per_layer * m.spec.n_layer + 2 + 1)
 
     def fetch(self) -> list[np.ndarray]:
         hist = self.history.cpu().numpy()

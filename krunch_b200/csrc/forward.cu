@@ -6,6 +6,7 @@
 #include <new>
 #include <vector>
 
+#include "model_impl.h"
 #include "profile.cuh"
 #include "rwkv_ops.cuh"
 
@@ -45,10 +46,6 @@ void prof_push(int phase, cudaEvent_t a, cudaEvent_t b, double work) {
 
 }  // namespace kb
 
-struct kb_model {
-    kb_model_desc d;
-    std::vector<kb_layer_desc> layers;
-};
 
 using namespace kb;
 

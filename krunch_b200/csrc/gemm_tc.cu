@@ -22,6 +22,7 @@
 
 #include <mutex>
 
+#include "epi_math.cuh"
 #include "rwkv_ops.cuh"
 #include "softmax_stats.cuh"
 #include "tc_common.cuh"
@@ -134,13 +135,11 @@ __device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* ou
         for (int h = 0; h < 4; ++h) {
             float y0 = u2f(acc[8 * j + 2 * h]), y1 = u2f(acc[8 * j + 2 * h + 1]);
             if (EPI == KB_EPI_SIGMOID) {
-                y0 = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-y0)));
-                y1 = __fdiv_rn(1.0f, __fadd_rn(1.0f, __expf(-y1)));
+                y0 = epi_sigmoid(y0);
+                y1 = epi_sigmoid(y1);
             } else if (EPI == KB_EPI_RELU_SQ) {
-                y0 = fmaxf(y0, 0.0f);
-                y1 = fmaxf(y1, 0.0f);
-                y0 = __fmul_rn(y0, y0);
-                y1 = __fmul_rn(y1, y1);
+                y0 = epi_relu_sq(y0);
+                y1 = epi_relu_sq(y1);
             } else if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID) {
                 const __half2 rr = *reinterpret_cast<const __half2*>(&rw[h]);
                 float g0 = 1.0f, g1 = 1.0f;
@@ -149,8 +148,8 @@ __device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* ou
                     g0 = __low2float(gg);
                     g1 = __high2float(gg);
                 }
-                y0 = __fmaf_rn(g0, y0, __low2float(rr));
-                y1 = __fmaf_rn(g1, y1, __high2float(rr));
+                y0 = epi_gate_resid(g0, y0, __low2float(rr));
+                y1 = epi_gate_resid(g1, y1, __high2float(rr));
             }
             const __half2 p = __floats2half2_rn(y0, y1);
             w[h] = *reinterpret_cast<const uint32_t*>(&p);
@@ -171,9 +170,8 @@ __device__ __forceinline__ void dequant32(uint32_t (&v)[32], float sa, const uin
         for (int h = 0; h < 4; ++h) {
             const float2 sw = __half22float2(*reinterpret_cast<const __half2*>(&qw[h]));
             const int c = 8 * j + 2 * h;
-            v[c] = __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int)v[c]), sa), sw.x));
-            v[c + 1] =
-                __float_as_uint(__fmul_rn(__fmul_rn(__int2float_rn((int)v[c + 1]), sa), sw.y));
+            v[c] = __float_as_uint(epi_dequant((int)v[c], sa, sw.x));
+            v[c + 1] = __float_as_uint(epi_dequant((int)v[c + 1], sa, sw.y));
         }
     }
 }

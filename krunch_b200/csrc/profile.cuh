@@ -7,7 +7,7 @@
 
 namespace kb {
 
-enum Phase { PH_EMBED = 0, PH_LN_MIX, PH_GEMM, PH_WKV, PH_HEAD, PH_CDF, PH_ENCODE, PH_DECODE, PH_N };
+enum Phase { PH_EMBED = 0, PH_LN_MIX, PH_GEMM, PH_WKV, PH_HEAD, PH_CDF, PH_ENCODE, PH_DECODE, PH_STEP, PH_N };
 
 bool prof_on();
 void prof_push(int phase, cudaEvent_t a, cudaEvent_t b, double work);

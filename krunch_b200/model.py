@@ -180,6 +180,29 @@ class RWKVModel:
     def new_stats(self, B: int, T: int) -> torch.Tensor:
         return torch.empty((B * T, self.stats_stride, 2), dtype=torch.float32, device=self.device)
 
+    # ------------------------------------------------------ fused decode step
+    @property
+    def has_fused_step(self) -> bool:
+        """The w8a8 model decodes through kb_step_forward (one persistent
+        launch for the layer stack)."""
+        return self.spec.wdtype == "i8"
+
+    def new_step_workspace(self, B: int) -> torch.Tensor:
+        n = int(N.load().kb_step_workspace_bytes(self.handle, B))
+        return torch.empty(n, dtype=torch.uint8, device=self.device)
+
+    def step_forward(self, tokens: torch.Tensor, state: torch.Tensor, workspace: torch.Tensor,
+                     logits: torch.Tensor, stats: torch.Tensor | None = None) -> torch.Tensor:
+        """forward_window for T = 1 through the fused step kernel (w8a8
+        models): the same bits as forward_window(tokens[:, None], ...)."""
+        B = tokens.shape[0]
+        assert tokens.dtype == torch.int32 and tokens.is_contiguous()
+        assert state.is_contiguous() and state.numel() == self.state_numel(B)
+        N.call("kb_step_forward", self.handle, tokens.data_ptr(), B, state.data_ptr(),
+               workspace.data_ptr(), workspace.numel(), logits.data_ptr(),
+               None if stats is None else stats.data_ptr(), N.stream_ptr(self.device))
+        return logits
+
     def forward_window(self, tokens: torch.Tensor, state: torch.Tensor, workspace: torch.Tensor,
                        logits: torch.Tensor, stats: torch.Tensor | None = None) -> torch.Tensor:
         """tokens int32 [B, T] (contiguous, on device) -> logits fp16 [B*T, vocab_pad].

@@ -166,3 +166,29 @@ def test_i8_codec_roundtrip(torch):
     back = codec.decompress_tokens(streams, [len(s) for s in seqs])
     for a, b in zip(seqs, back):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("shape,B", [((2, 128, 512, 300), 3), ((2, 128, 512, 300), 300),
+                                     ((12, 768, 3072, 50277), 256), ((12, 768, 3072, 50277), 5)])
+def test_fused_step_matches_window_forward(torch, shape, B):
+    """kb_step_forward (one persistent launch per step) == kb_forward_window
+    with T = 1, bit for bit, logits, softmax partials and state, over
+    several steps."""
+    from krunch_b200 import _native as N
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(*shape, seed=11), wdtype="i8")
+    V = shape[3]
+    rng = np.random.default_rng(B)
+    st_a, st_b = m.new_state(B), m.new_state(B)
+    ws_a, ws_b = m.new_workspace(B, 1), m.new_step_workspace(B)
+    for step in range(3):
+        tok = torch.from_numpy(rng.integers(0, V, B).astype(np.int32)).cuda()
+        la, lb = m.new_logits(B, 1), m.new_logits(B, 1)
+        sa, sb = m.new_stats(B, 1), m.new_stats(B, 1)
+        m.forward_window(tok.view(B, 1), st_a, ws_a, la, sa)
+        m.step_forward(tok, st_b, ws_b, lb, sb)
+        torch.cuda.synchronize()
+        N.call("kb_step_error_status", 1)  # raises if a bounded wait expired
+        assert torch.equal(la, lb), step
+        assert torch.equal(sa, sb), step
+        assert torch.equal(st_a, st_b), step
