@@ -142,6 +142,69 @@ def run_reference(args):
     }))
 
 
+def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
+    """w8a8 RWKV-4-169M, B streams decoded in lock-step, one token
+    per stream per step (fused step kernel + head + decode kernel per step,
+    replayed as a CUDA graph).  Streams are compressed first by the packed
+    path of the same int8 model; the decoded tokens must equal the input."""
+    import torch
+    from krunch_b200.codec import Codec, DecompressPlan
+    from krunch_b200.model import RWKVModel
+    from krunch_b200.synth import random_weights, zipf_tokens
+    Bd, Td = args.dec_B, args.dec_T
+    model = RWKVModel(random_weights(**SHAPE, seed=0), device=stream.device, wdtype="i8")
+    codec = Codec(model, cdf_bits=args.cdf_bits)
+    seqs = list(zipf_tokens((Bd, Td), seed=100 + rank))
+    streams = codec.compress_tokens(seqs)
+    lens = [len(s) for s in streams]
+    dp = DecompressPlan(codec, lens, [Td] * Bd)
+    dp.upload(streams)
+    dp.run()  # warm-up, graph capture
+    torch.cuda.synchronize()
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(stream.device.index) as clk:
+        d0.record(stream)
+        dp.run()
+        d1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    dms = max_over_ranks(d0.elapsed_time(d1))
+    ok = all(np.array_equal(a, b) for a, b in zip(dp.fetch(), seqs))
+    # end to end through the plan API: bitstreams from pinned host memory in,
+    # tokens out, inside the timed region
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dp2 = DecompressPlan(codec, lens, [Td] * Bd)
+    dp2.upload(streams)
+    dp2.run()
+    out = dp2.fetch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = max_over_ranks(e0.elapsed_time(e1))
+    ok = ok and all(np.array_equal(a, b) for a, b in zip(out, seqs))
+    sp = SHAPE
+    C, F, L, V = sp["n_embd"], sp["n_ffn"], sp["n_layer"], sp["n_vocab"]
+    w_bytes = L * (5 * C * C + 2 * C * F) + C * V          # int8 weights read per step
+    s_bytes = 2 * L * 5 * Bd * C * 4                        # fp32 state read + written
+    us = dms * 1e3 / Td
+    pk, pk_kind = peaks()
+    ach = (w_bytes + s_bytes) / (us * 1e-6) / 1e9
+    tok = Bd * Td * world
+    return {"workload": f"configs[2] decompress: w8a8 RWKV-4-169M, B={Bd} x {Td} steps per GPU, "
+                        "fp32 state, CUDA graph of (fused step, head, decode) per step",
+            "value": tok * BYTES_PER_TOKEN / (dms / 1e3) / 1e6, "unit": "MB/s",
+            "us_per_step": us, "byte_exact": bool(ok), "gpu_launches_per_step": 4,
+            "bits_per_token": 8.0 * sum(lens) / (Bd * Td),
+            "roofline": {"bound": "hbm", "achieved": ach, "unit": "GB/s", "peak": pk["hbm_gbs"],
+                         "peak_kind": pk_kind, "frac": ach / pk["hbm_gbs"],
+                         "algorithmic_bytes_per_step": w_bytes + s_bytes},
+            "e2e": {"value": tok * BYTES_PER_TOKEN / (ems / 1e3) / 1e6, "unit": "MB/s",
+                    "h2d_bytes_per_step": dp2.h2d_bytes, "d2h_bytes_per_step": dp2.d2h_bytes},
+            "clocks": clk.summary()}
+
+
 def config(args):
     return {"workload": "configs[1] compress, packed forward, 1 GPU per rank",
             "model": "RWKV-4-169M random-init fp16", "chunks_per_gpu": args.B,
@@ -164,8 +227,10 @@ def main():
     ap.add_argument("--ref-chunks", type=int, default=4)
     ap.add_argument("--ref-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--decompress", action="store_true",
-                    help="also time configs[2]-shaped decompress (fp16 weights)")
+    ap.add_argument("--no-decompress", action="store_true",
+                    help="skip the configs[2] decompress line (w8a8, B=256 x 2048 steps)")
+    ap.add_argument("--dec-B", type=int, default=256)
+    ap.add_argument("--dec-T", type=int, default=2048)
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -272,26 +337,8 @@ def main():
            "wall_ms_per_step": wall_ms}
 
     extra = {}
-    if args.decompress:
-        from krunch_b200.codec import DecompressPlan
-        Bd, Td = 256, 2048
-        dseqs = list(zipf_tokens((Bd, Td), seed=100 + rank))
-        dstreams = codec.compress_tokens(dseqs)
-        dp = DecompressPlan(codec, [len(s) for s in dstreams], [Td] * Bd)
-        dp.upload(dstreams)
-        dp.run()  # warm-up + graph capture
-        torch.cuda.synchronize()
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record(stream)
-        dp.run()
-        d1.record(stream)
-        torch.cuda.synchronize()
-        dms = max_over_ranks(d0.elapsed_time(d1))
-        ok = all(np.array_equal(a, b) for a, b in zip(dp.fetch(), dseqs))
-        extra["decompress"] = {
-            "workload": "configs[2] shape (B=256 x 2048 steps), fp16 weights (int8 not built)",
-            "value": Bd * Td * world * BYTES_PER_TOKEN / (dms / 1e3) / 1e6, "unit": "MB/s",
-            "us_per_step": dms * 1e3 / Td, "byte_exact": ok}
+    if not args.no_decompress:
+        extra["decompress"] = bench_decompress(args, rank, world, stream, max_over_ranks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

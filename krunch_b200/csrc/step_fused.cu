@@ -120,9 +120,11 @@ __device__ bool grid_sync(const SfParams& p, SfBars* sb, unsigned epoch) {
     __syncthreads();
     if (threadIdx.x == 0 && blockIdx.x == 0 && p.trace) p.trace[2 * epoch] = gtimer();
     if (threadIdx.x == 0) {
-        __threadfence();
+        // release: the CTA's writes (ordered before this thread by the
+        // __syncthreads above) become visible with the arrival; the proxy
+        // fences order them with the TMA reads of the next tile phase
         fence_proxy_async_global();
-        atomicAdd(p.bar, 1u);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         int ok = 1;
         const unsigned long long t0 = gtimer();
@@ -140,7 +142,6 @@ __device__ bool grid_sync(const SfParams& p, SfBars* sb, unsigned epoch) {
                 }
             }
         }
-        __threadfence();
         fence_proxy_async_global();
         sb->ok = ok;
         if (blockIdx.x == 0 && p.trace) p.trace[2 * epoch + 1] = gtimer();
