@@ -233,6 +233,18 @@ __device__ __forceinline__ int counts8(const float (&e)[8], float g, int i0, int
     return sum;
 }
 
+// Counts of 8 consecutive in-range elements: floor via the round-down
+// conversion (the same value as (int)floorf for these magnitudes).
+__device__ __forceinline__ int counts8_full(const float (&e)[8], float g, int (&c)[8]) {
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        c[k] = __float2int_rd(__fmul_rn(e[k], g)) + 1;
+        sum += c[k];
+    }
+    return sum;
+}
+
 __device__ __forceinline__ void unpack8(const uint4& q, float (&e)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&q);
 #pragma unroll
@@ -255,6 +267,10 @@ struct NumSrc {
             for (int k = 0; k < 8; ++k) e[k] = (i0 + k < lim) ? h2f(x[i0 + k]) : 0.0f;
         }
     }
+    // i0 + 8 <= V and x + i0 16-byte aligned (row starts 16-byte aligned)
+    __device__ __forceinline__ void load8_full(int i0, float (&e)[8]) const {
+        unpack8(*reinterpret_cast<const uint4*>(x + i0), e);
+    }
     __device__ __forceinline__ bool is_one(int i) const {
         return i < V && x[i] == (uint16_t)0x3C00u;
     }
@@ -271,6 +287,7 @@ struct RawSrc {
         for (int k = 0; k < 8; ++k)
             e[k] = (i0 + k < lim) ? h2f(exp_rel_f16(h2f(x[i0 + k]), m)) : 0.0f;
     }
+    __device__ __forceinline__ void load8_full(int i0, float (&e)[8]) const { load8(i0, i0 + 8, e); }
     __device__ __forceinline__ bool is_one(int i) const {
         return i < V && exp_rel_f16(h2f(x[i]), part[i / SUBTILE].x) == (uint16_t)0x3C00u;
     }
@@ -302,8 +319,13 @@ __device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int
         int c[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ls = 0;
         if (i0 < we) {
             float e[8];
-            src.load8(i0, we, e);
-            ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+            if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
+                src.load8_full(i0, e);
+                ls = counts8_full(e, gs[i0 / SUBTILE], c);
+            } else {
+                src.load8(i0, we, e);
+                ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+            }
 #pragma unroll
             for (int k = 0; k < 8; ++k)
                 if (i0 + k == amax) c[k] += deficit;
@@ -336,14 +358,21 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
     if (MODE == MODE_DECODE && tid == 0) s_target = decode_target(states + 4 * (int64_t)row, bits);
 
     // ---- element pass: totals (and the prefix below the symbol) ----------
+    const bool aligned_row = (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0;
     int cs = 0, below = 0;
     for (int base = wa; base < we; base += 256) {
         const int i0 = base + lane * 8;
         if (i0 >= we) continue;
         float e[8];
         int c[8];
-        src.load8(i0, we, e);
-        const int step = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+        int step;
+        if (i0 + 8 <= we && aligned_row) {
+            src.load8_full(i0, e);
+            step = counts8_full(e, gs[i0 / SUBTILE], c);
+        } else {
+            src.load8(i0, we, e);
+            step = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+        }
         cs += step;
         if (MODE == MODE_LOHI) {
             if (i0 + 8 <= sym) {

@@ -13,11 +13,13 @@
 
 namespace kb {
 
-// LN + token-shift mix, one warp per row, every row independent:
-//   prev(t) = state_in[b] for t == 0, else LN(x[t-1]) recomputed by this warp
+// LN + token-shift mix, one warp per strip of `rpw` consecutive rows:
+//   prev(t) = state_in[b] for t == 0, else LN(x[t-1]) (carried from the
+//             previous row of the strip, recomputed for the strip's first)
 //   mix_j   = xx * m_j + prev * (1 - m_j)   (rwkv4_step_ref.py:59-61)
-// Row index = b*T + t.  The stream's last row writes its xx to state_out[b];
-// xx_out (optional) receives xx.
+// Row index = b*T + t.  Every LN is the same function of its row alone, so
+// the strip length changes no bits.  The stream's last row writes its xx to
+// state_out[b]; xx_out (optional) receives xx.
 template <int NMIX, int EPL>
 __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __restrict__ x, int B,
                                                           int T, int C,
@@ -25,44 +27,52 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
                                                           const float* __restrict__ lb, MixArgs ma,
                                                           const float* __restrict__ state_in,
                                                           float* __restrict__ state_out,
-                                                          uint16_t* __restrict__ xx_out) {
+                                                          uint16_t* __restrict__ xx_out, int rpw) {
     const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
-    if (row >= (int64_t)B * T) return;
-    const int b = (int)(row / T);
-    const int t = (int)(row - (int64_t)b * T);
-
-    float v[EPL], cur[EPL], prev[EPL];
-    load_row<EPL>(x + row * C, lane, v);
-    if (NMIX > 0) {
-        if (t == 0) {
+    const int64_t rows = (int64_t)B * T;
+    const int64_t r0 = ((int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5)) * rpw;
+    float prev[EPL], cur[EPL];
+    for (int j = 0; j < rpw; ++j) {
+        const int64_t row = r0 + j;
+        if (row >= rows) return;
+        const int b = (int)(row / T);
+        const int t = (int)(row - (int64_t)b * T);
+        float v[EPL];
+        load_row<EPL>(x + row * C, lane, v);
+        if (NMIX > 0) {
+            if (t == 0) {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e)
+                    prev[e] = state_in ? state_in[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] : 0.0f;
+            } else if (j == 0) {
+                float pv[EPL];
+                load_row<EPL>(x + (row - 1) * C, lane, pv);
+                ln_warp<EPL>(pv, C, lane, lw, lb, prev);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPL; ++e) prev[e] = cur[e];
+            }
+        }
+        ln_warp<EPL>(v, C, lane, lw, lb, cur);
+        if (xx_out) store_row_f16<EPL>(xx_out + row * C, lane, cur);
+        if (NMIX == 0 && ma.q[0]) store_row_q<EPL>(ma.q[0] + row * C, ma.qs[0] + row, lane, cur);
+#pragma unroll
+        for (int m = 0; m < NMIX; ++m) {
+            float mk[EPL];
+            load_vec_f32<EPL>(ma.mix[m], lane, mk);
 #pragma unroll
             for (int e = 0; e < EPL; ++e)
-                prev[e] = state_in ? state_in[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] : 0.0f;
-        } else {
-            float pv[EPL];
-            load_row<EPL>(x + (row - 1) * C, lane, pv);
-            ln_warp<EPL>(pv, C, lane, lw, lb, prev);
+                mk[e] = __fmaf_rn(cur[e], mk[e], __fmul_rn(prev[e], __fsub_rn(1.0f, mk[e])));
+            if (ma.q[m])
+                store_row_q<EPL>(ma.q[m] + row * C, ma.qs[m] + row, lane, mk);
+            else
+                store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
         }
-    }
-    ln_warp<EPL>(v, C, lane, lw, lb, cur);
-    if (xx_out) store_row_f16<EPL>(xx_out + row * C, lane, cur);
-    if (NMIX == 0 && ma.q[0]) store_row_q<EPL>(ma.q[0] + row * C, ma.qs[0] + row, lane, cur);
+        if (t == T - 1 && state_out) {
 #pragma unroll
-    for (int m = 0; m < NMIX; ++m) {
-        float mk[EPL];
-        load_vec_f32<EPL>(ma.mix[m], lane, mk);
-#pragma unroll
-        for (int e = 0; e < EPL; ++e)
-            mk[e] = __fmaf_rn(cur[e], mk[e], __fmul_rn(prev[e], __fsub_rn(1.0f, mk[e])));
-        if (ma.q[m])
-            store_row_q<EPL>(ma.q[m] + row * C, ma.qs[m] + row, lane, mk);
-        else
-            store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
-    }
-    if (t == T - 1 && state_out) {
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) state_out[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] = cur[e];
+            for (int e = 0; e < EPL; ++e)
+                state_out[(int64_t)b * C + RowIdx<EPL>::col(lane, e)] = cur[e];
+        }
     }
 }
 
@@ -228,13 +238,13 @@ int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, 
 }
 
 template <int NMIX>
-static int ln_mix_epl(int epl, int blocks, cudaStream_t st, const uint16_t* x, int B, int T, int C,
+static int ln_mix_epl(int epl, int blocks, int rpw, cudaStream_t st, const uint16_t* x, int B, int T, int C,
                       const float* lw, const float* lb, const MixArgs& ma, const float* state_in,
                       float* state_out, uint16_t* xx_out) {
 #define KB_LN_CASE(E)                                                                           \
     case E:                                                                                     \
         k_ln_mix<NMIX, E><<<blocks, LN_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in,   \
-                                                            state_out, xx_out);                 \
+                                                            state_out, xx_out, rpw);            \
         return KB_OK;
     switch (epl) {
         KB_LN_CASE(4) KB_LN_CASE(8) KB_LN_CASE(16) KB_LN_CASE(24) KB_LN_CASE(32) KB_LN_CASE(48)
@@ -251,12 +261,14 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
     if (C % 32) return KB_ERR_SHAPE;
     const int epl = C / 32;
     const int64_t rows = (int64_t)B * T;
-    const int blocks = (int)((rows + LN_WARPS - 1) / LN_WARPS);
+    // strips of 4 rows once there are enough rows to fill the GPU many times
+    const int rpw = rows >= (int64_t)148 * LN_WARPS * 64 ? 4 : 1;
+    const int blocks = (int)((rows + LN_WARPS * rpw - 1) / (LN_WARPS * rpw));
     int rc;
     switch (nmix) {
-        case 0: rc = ln_mix_epl<0>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
-        case 2: rc = ln_mix_epl<2>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
-        case 3: rc = ln_mix_epl<3>(epl, blocks, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 0: rc = ln_mix_epl<0>(epl, blocks, rpw, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 2: rc = ln_mix_epl<2>(epl, blocks, rpw, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
+        case 3: rc = ln_mix_epl<3>(epl, blocks, rpw, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
         default: return KB_ERR_ARG;
     }
     if (rc != KB_OK) return rc;

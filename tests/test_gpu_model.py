@@ -95,3 +95,16 @@ def test_production_convention_vs_oracle(torch):
     lg, _ = _run(torch, m, tok)
     ref, _ = rwkv.forward(w, tok, wkv="production")
     assert np.abs(lg - ref).max() <= LOGIT_TOL
+
+
+def test_large_window_strips_match_small(torch):
+    """Windows of >= 75776 rows run LayerNorm+mix in strips of 4 rows per
+    warp; a stream's logits must equal the same stream run alone (1 row per
+    warp)."""
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=8))
+    tok = np.random.default_rng(3).integers(0, 300, (76, 1000))
+    big, st_big = _run(torch, m, tok)
+    for b in (0, 37, 75):
+        one, st_one = _run(torch, m, tok[b:b + 1])
+        assert np.array_equal(one[0], big[b]), b
