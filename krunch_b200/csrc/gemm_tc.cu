@@ -31,6 +31,7 @@ namespace kb {
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_NT = 576;
 constexpr int TC_EPI_WARPS = 16;
+constexpr uint32_t TC_STAGE_OUT = 2048;  // output staging per epilogue warp
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 
 // Tile width BN in {256, 128, 64, 32}: 256 for large M; narrower tiles give
@@ -47,7 +48,10 @@ struct TcCfg {
     static constexpr uint32_t STAGE_BYTES = TC_A_BYTES + B_BYTES;
     static constexpr int STAGES = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
-    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*bars*/;
+    static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES +
+                                   TC_EPI_WARPS * TC_STAGE_OUT /*output staging*/ +
+                                   1024 /*align*/ + 256 /*bars*/;
+    static_assert(SMEM <= 232448, "shared memory per block");
     static constexpr uint32_t IDESC =
         KIND == TC_I8 ? tc::idesc_i8(TC_BM, BN) : tc::idesc_f16(TC_BM, BN, false);
 };
@@ -100,35 +104,53 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m0
     n0 = (r / gm) * BN;
 }
 
-// Epilogue on 32 consecutive columns [c0, c0+32) of row r.
-template <int EPI>
-__device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* out, int64_t ldo,
-                                             const uint16_t* resid, const uint16_t* gate,
-                                             int64_t r, int c0) {
-    const int64_t o = r * ldo + c0;
-    if (EPI == KB_EPI_F32) {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + o);
+// Output staging: each epilogue warp owns 2 KB of shared memory holding a
+// 32-row x 64-byte tile in the 64-byte swizzle TMA expects (16-byte chunk j
+// of row r at chunk position j ^ ((r >> 1) & 3)); one elected lane writes the
+// tile to global memory with a TMA store.  Rows past M are clipped by TMA.
+__device__ __forceinline__ void stage_row64(unsigned char* st, int r, const uint32_t (&w)[16]) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(u2f(acc[4 * j]), u2f(acc[4 * j + 1]), u2f(acc[4 * j + 2]),
-                                 u2f(acc[4 * j + 3]));
-        return;
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<uint4*>(st + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) =
+            make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+// Warp-wide: wait until the staging tile is free, stage this lane's row,
+// store the tile at (c0, r0).
+__device__ __forceinline__ void stage_and_store(unsigned char* st, int lane,
+                                                const uint32_t (&w)[16], const CUtensorMap* map,
+                                                int c0, int r0) {
+    if (lane == 0) tc::bulk_wait_read();
+    __syncwarp();
+    stage_row64(st, lane, w);
+    tc::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tc::tma_store_2d(map, st, c0, r0);
+        tc::bulk_commit();
     }
+}
+
+// Epilogue values of 32 consecutive columns [c0, c0+32) of row r, as 16
+// words of fp16 pairs (non-F32 epilogues); resid/gate read only if `valid`.
+template <int EPI>
+__device__ __forceinline__ void tc_epi_pack(const uint32_t (&acc)[32], int64_t ldo,
+                                            const uint16_t* resid, const uint16_t* gate,
+                                            int64_t r, int c0, bool valid, uint32_t (&w)[16]) {
+    const int64_t o = r * ldo + c0;
     uint4 rv[4], gv[4];
     if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID) {
         const uint4* rs = reinterpret_cast<const uint4*>(resid + o);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) rv[j] = rs[j];
+        for (int j = 0; j < 4; ++j) rv[j] = valid ? rs[j] : make_uint4(0, 0, 0, 0);
     }
     if (EPI == KB_EPI_GATE_RESID) {
         const uint4* gs = reinterpret_cast<const uint4*>(gate + o);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) gv[j] = gs[j];
+        for (int j = 0; j < 4; ++j) gv[j] = valid ? gs[j] : make_uint4(0, 0, 0, 0);
     }
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        uint32_t w[4];
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
         const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gv[j]);
 #pragma unroll
@@ -152,9 +174,8 @@ __device__ __forceinline__ void tc_epi_store(const uint32_t (&acc)[32], void* ou
                 y1 = epi_gate_resid(g1, y1, __high2float(rr));
             }
             const __half2 p = __floats2half2_rn(y0, y1);
-            w[h] = *reinterpret_cast<const uint32_t*>(&p);
+            w[4 * j + h] = *reinterpret_cast<const uint32_t*>(&p);
         }
-        dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 
@@ -179,7 +200,7 @@ __device__ __forceinline__ void dequant32(uint32_t (&v)[32], float sa, const uin
 template <int EPI, int BN, int KIND>
 __global__ void __launch_bounds__(TC_NT, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const __grid_constant__ TcArgs args) {
+              const __grid_constant__ CUtensorMap mapO, const __grid_constant__ TcArgs args) {
     using Cfg = TcCfg<BN, KIND>;
     const int M = args.M, N = args.N, K = args.K;
     void* const out = args.out;
@@ -191,7 +212,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
     extern __shared__ unsigned char tc_smem_raw[];
     const uint32_t raw = tc::smem_addr(tc_smem_raw);
     unsigned char* smem = tc_smem_raw + (((raw + 1023u) & ~1023u) - raw);
-    TcBars* bars = reinterpret_cast<TcBars*>(smem + TC_STAGES * TC_STAGE_BYTES);
+    unsigned char* stage_out = smem + TC_STAGES * TC_STAGE_BYTES;  // 16 x TC_STAGE_OUT
+    TcBars* bars = reinterpret_cast<TcBars*>(stage_out + TC_EPI_WARPS * TC_STAGE_OUT);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_n = (N + BN - 1) / BN;
@@ -214,6 +236,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
     if (warp == 0 && lane == 0) {
         tc::prefetch_tmap(&mapA);
         tc::prefetch_tmap(&mapB);
+        tc::prefetch_tmap(&mapO);
     }
     if (warp == 1) tc::tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
     tc::fence_before_sync();
@@ -300,6 +323,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
         // ---------------- epilogue (warps 2..17) ----------------
         const int q = warp & 3;          // TMEM lane quadrant this warp may access
         const int g = (warp - 2) >> 2;   // quarter of the tile's columns
+        unsigned char* st = stage_out + (warp - 2) * TC_STAGE_OUT;
         int i = 0;
         for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
             const int a = i & 1;
@@ -368,13 +392,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
                             packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
                         }
                     }
+                    stage_and_store(st, lane, packed, &mapO, col0, m0 + q * 32);
                     if (row < M) {
-                        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) +
-                                                              row * ldo + col0);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j)
-                            dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                                                packed[4 * j + 3]);
                         const int u = col0 / SUBTILE;
                         if (u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
                     }
@@ -388,13 +407,26 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
                     tc::tmem_ld_wait();
                     if (KIND == TC_I8) dequant32(v, sa, args.w_scale + col0);
-                    if (row < M) tc_epi_store<EPI>(v, out, ldo, args.resid, args.gate, row, col0);
+                    if (EPI == KB_EPI_F32) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {  // two 16-column (64-byte) halves
+                            uint32_t w[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) w[j] = v[16 * h + j];
+                            stage_and_store(st, lane, w, &mapO, col0 + 16 * h, m0 + q * 32);
+                        }
+                    } else {
+                        uint32_t w[16];
+                        tc_epi_pack<EPI>(v, ldo, args.resid, args.gate, row, col0, row < M, w);
+                        stage_and_store(st, lane, w, &mapO, col0, m0 + q * 32);
+                    }
                 }
             }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bars->tempty[a]);
         }
+        if (lane == 0) tc::bulk_wait_all();  // staged stores done before exit
     }
 
     tc::fence_before_sync();
@@ -440,6 +472,21 @@ bool make_map(CUtensorMap* map, const void* base, int rows, int cols, int64_t ld
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Output [rows, cols] (fp32: elem 4, fp16: elem 2), row stride ld elements,
+// box 64 bytes x 32 rows with the 64-byte swizzle of the staging tiles.
+bool make_out_map(CUtensorMap* map, void* base, int rows, int cols, int64_t ld, int elem) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * elem};
+    cuuint32_t box[2] = {(cuuint32_t)(64 / elem), 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, elem == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+              base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int sm_count() {
     static int cache[64] = {};
     int dev = 0;
@@ -467,12 +514,13 @@ int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs
         set_cuda_error(attr_err);
         return KB_ERR_CUDA;
     }
-    CUtensorMap mb;
-    if (!make_map(&mb, W, args.N, args.K, ldw, BN, KIND == TC_I8 ? 1 : 2))
+    CUtensorMap mb, mo;
+    if (!make_map(&mb, W, args.N, args.K, ldw, BN, KIND == TC_I8 ? 1 : 2) ||
+        !make_out_map(&mo, args.out, args.M, args.N, args.ldo, EPI == KB_EPI_F32 ? 4 : 2))
         return KB_ERR_UNSUPPORTED;
     const int tiles = ((args.M + TC_BM - 1) / TC_BM) * ((args.N + BN - 1) / BN);
     const int grid = tiles < sm_count() ? tiles : sm_count();
-    k_gemm_tc<EPI, BN, KIND><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, args);
+    k_gemm_tc<EPI, BN, KIND><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, mo, args);
     return launch_status();
 }
 
