@@ -131,24 +131,33 @@ __device__ __forceinline__ void stage_and_store(unsigned char* st, int lane,
     }
 }
 
-// Epilogue values of 32 consecutive columns [c0, c0+32) of row r, as 16
-// words of fp16 pairs (non-F32 epilogues); resid/gate read only if `valid`.
+// Warp-wide coalesced read of a 32-row x 32-column fp16 tile (rows from r0,
+// rows >= M read as zero) through the staging buffer; lane i gets row r0 + i.
+__device__ __forceinline__ void load_tile_rows(const uint16_t* src, int64_t ld, int64_t r0, int c0,
+                                               int M, unsigned char* st, int lane,
+                                               uint4 (&out)[4]) {
+    if (lane == 0) tc::bulk_wait_read();
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int idx = k * 32 + lane, r = idx >> 2, j = idx & 3;
+        const int64_t gr = r0 + r;
+        const uint4 v = gr < M ? *reinterpret_cast<const uint4*>(src + gr * ld + c0 + j * 8)
+                               : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(st + r * 64 + ((j ^ ((r >> 1) & 3)) << 4)) = v;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        out[j] = *reinterpret_cast<const uint4*>(st + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
+    __syncwarp();
+}
+
+// Epilogue values of 32 consecutive columns of one row as 16 words of fp16
+// pairs (non-F32 epilogues); rv / gv: the row's residual / gate values.
 template <int EPI>
-__device__ __forceinline__ void tc_epi_pack(const uint32_t (&acc)[32], int64_t ldo,
-                                            const uint16_t* resid, const uint16_t* gate,
-                                            int64_t r, int c0, bool valid, uint32_t (&w)[16]) {
-    const int64_t o = r * ldo + c0;
-    uint4 rv[4], gv[4];
-    if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID) {
-        const uint4* rs = reinterpret_cast<const uint4*>(resid + o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) rv[j] = valid ? rs[j] : make_uint4(0, 0, 0, 0);
-    }
-    if (EPI == KB_EPI_GATE_RESID) {
-        const uint4* gs = reinterpret_cast<const uint4*>(gate + o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) gv[j] = valid ? gs[j] : make_uint4(0, 0, 0, 0);
-    }
+__device__ __forceinline__ void tc_epi_pack(const uint32_t (&acc)[32], const uint4 (&rv)[4],
+                                            const uint4 (&gv)[4], uint32_t (&w)[16]) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         const uint32_t* rw = reinterpret_cast<const uint32_t*>(&rv[j]);
@@ -203,7 +212,6 @@ __global__ void __launch_bounds__(TC_NT, 1)
               const __grid_constant__ CUtensorMap mapO, const __grid_constant__ TcArgs args) {
     using Cfg = TcCfg<BN, KIND>;
     const int M = args.M, N = args.N, K = args.K;
-    void* const out = args.out;
     const int64_t ldo = args.ldo;
     const int V = args.V, stats_stride = args.stats_stride;
     float2* const stats = args.stats;
@@ -417,7 +425,12 @@ __global__ void __launch_bounds__(TC_NT, 1)
                         }
                     } else {
                         uint32_t w[16];
-                        tc_epi_pack<EPI>(v, ldo, args.resid, args.gate, row, col0, row < M, w);
+                        uint4 rv[4], gv[4];
+                        if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID)
+                            load_tile_rows(args.resid, ldo, m0 + q * 32, col0, M, st, lane, rv);
+                        if (EPI == KB_EPI_GATE_RESID)
+                            load_tile_rows(args.gate, ldo, m0 + q * 32, col0, M, st, lane, gv);
+                        tc_epi_pack<EPI>(v, rv, gv, w);
                         stage_and_store(st, lane, w, &mapO, col0, m0 + q * 32);
                     }
                 }
