@@ -95,26 +95,48 @@ __global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float
     const float* vp = v + base;
     const uint16_t* rp = r + base;
     uint16_t* op = ry + base;
-    int t0 = 0;
-    for (; t0 + WKV_BLK <= T; t0 += WKV_BLK) {
-        float kb[WKV_BLK], vb[WKV_BLK];
-        uint16_t rb[WKV_BLK];
+    // blocks of WKV_BLK steps; the next block's loads are in flight while
+    // the current block is computed
+    const int nblk = T / WKV_BLK;
+    float kb[WKV_BLK], vb[WKV_BLK];
+    uint16_t rb[WKV_BLK];
+    if (nblk > 0) {
 #pragma unroll
         for (int j = 0; j < WKV_BLK; ++j) {
-            kb[j] = __ldg(kp);
-            vb[j] = __ldg(vp);
-            rb[j] = __ldg(rp);
-            kp += C;
-            vp += C;
-            rp += C;
+            kb[j] = __ldg(kp + (int64_t)j * C);
+            vb[j] = __ldg(vp + (int64_t)j * C);
+            rb[j] = __ldg(rp + (int64_t)j * C);
+        }
+    }
+    for (int ib = 0; ib < nblk; ++ib) {
+        float kn[WKV_BLK], vn[WKV_BLK];
+        uint16_t rn[WKV_BLK];
+        const int64_t nx = (int64_t)WKV_BLK * C;
+        if (ib + 1 < nblk) {
+#pragma unroll
+            for (int j = 0; j < WKV_BLK; ++j) {
+                kn[j] = __ldg(kp + nx + (int64_t)j * C);
+                vn[j] = __ldg(vp + nx + (int64_t)j * C);
+                rn[j] = __ldg(rp + nx + (int64_t)j * C);
+            }
         }
 #pragma unroll
         for (int j = 0; j < WKV_BLK; ++j) {
             const float y = wkv_step<CONV>(aa, bb, pp, kb[j], vb[j], u, dec);
-            *op = f2h(__fmul_rn(h2f(rb[j]), y));
-            op += C;
+            op[(int64_t)j * C] = f2h(__fmul_rn(h2f(rb[j]), y));
         }
+#pragma unroll
+        for (int j = 0; j < WKV_BLK; ++j) {
+            kb[j] = kn[j];
+            vb[j] = vn[j];
+            rb[j] = rn[j];
+        }
+        kp += nx;
+        vp += nx;
+        rp += nx;
+        op += nx;
     }
+    int t0 = nblk * WKV_BLK;
     for (; t0 < T; ++t0) {
         const float y = wkv_step<CONV>(aa, bb, pp, __ldg(kp), __ldg(vp), u, dec);
         *op = f2h(__fmul_rn(h2f(__ldg(rp)), y));
