@@ -235,11 +235,16 @@ __device__ __forceinline__ int counts8(const float (&e)[8], float g, int i0, int
 
 // Counts of 8 consecutive in-range elements: floor via the round-down
 // conversion (the same value as (int)floorf for these magnitudes).
+// SMALL (T - V < 2^23): floor(q) as the low bits of q + 2^23 rounded down,
+// which is exact for 0 <= q < 2^23 and stays in the full-rate FP/INT pipes.
+template <bool SMALL>
 __device__ __forceinline__ int counts8_full(const float (&e)[8], float g, int (&c)[8]) {
     int sum = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-        c[k] = __float2int_rd(__fmul_rn(e[k], g)) + 1;
+        const float q = __fmul_rn(e[k], g);
+        c[k] = (SMALL ? (__float_as_int(__fadd_rd(q, 8388608.0f)) - 0x4B000000)
+                      : __float2int_rd(q)) + 1;
         sum += c[k];
     }
     return sum;
@@ -312,7 +317,7 @@ __device__ __forceinline__ void raw_partials(const uint16_t* x, int V, int nsub,
 // true stops the walk.
 template <class Src, class F>
 __device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int wa, int we,
-                                            int amax, int deficit, F f) {
+                                            int amax, int deficit, bool small, F f) {
     const int lane = threadIdx.x & 31;
     for (int base = wa; base < we; base += 256) {
         const int i0 = base + lane * 8;
@@ -321,7 +326,8 @@ __device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int
             float e[8];
             if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
                 src.load8_full(i0, e);
-                ls = counts8_full(e, gs[i0 / SUBTILE], c);
+                ls = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
+                           : counts8_full<false>(e, gs[i0 / SUBTILE], c);
             } else {
                 src.load8(i0, we, e);
                 ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
@@ -359,6 +365,7 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
 
     // ---- element pass: totals (and the prefix below the symbol) ----------
     const bool aligned_row = (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0;
+    const bool small = (T - V) < (1 << 23);
     int cs = 0, below = 0;
     for (int base = wa; base < we; base += 256) {
         const int i0 = base + lane * 8;
@@ -368,7 +375,8 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         int step;
         if (i0 + 8 <= we && aligned_row) {
             src.load8_full(i0, e);
-            step = counts8_full(e, gs[i0 / SUBTILE], c);
+            step = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
+                         : counts8_full<false>(e, gs[i0 / SUBTILE], c);
         } else {
             src.load8(i0, we, e);
             step = counts8(e, gs[i0 / SUBTILE], i0, we, c);
@@ -416,7 +424,7 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         int32_t* o = reinterpret_cast<int32_t*>(out) + (int64_t)row * (V + 1);
         if (tid == 0) o[0] = 0;
         int run = s_wexcl[warp];
-        walk_counts(src, gs, wa, we, amax, deficit,
+        walk_counts(src, gs, wa, we, amax, deficit, small,
                     [&](int i0, const int (&c)[8], int, int excl, int total) {
                         if (i0 < we) {
                             int r = run + excl;
@@ -442,7 +450,7 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
     __syncthreads();
     if (warp == s_owner) {
         int run = s_wexcl[warp];
-        walk_counts(src, gs, wa, we, amax, deficit,
+        walk_counts(src, gs, wa, we, amax, deficit, small,
                     [&](int i0, const int (&c)[8], int ls, int excl, int total) {
                         if (target >= (uint32_t)(run + total)) {
                             run += total;

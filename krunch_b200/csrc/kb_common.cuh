@@ -41,7 +41,7 @@ constexpr uint32_t RC_THREE_QTR = RC_HALF + RC_QTR;
 // restatement reproduces it bit for bit.
 //
 // Method: e^x = 2^y with y = x * log2(e) (one rounding); y = n + f with
-// n = rint(y), |f| <= 1/2; 2^f by the degree-5 Taylor polynomial of
+// n = rint(y) (ties to even), |f| <= 1/2; 2^f by the degree-5 Taylor polynomial of
 // e^(f ln 2) in Horner form (truncation < 2.6e-6 relative); 2^n added to the
 // exponent field.  Relative error below 7e-6 over the domain.  Inputs below
 // -86 return 0 (so every result is a normal number and flush-to-zero
@@ -61,7 +61,11 @@ __device__ __forceinline__ float kb_expf(float x) {
     if (!(x >= -86.0f)) return 0.0f;
     const float LOG2E = kb_bits_to_float(0x3fb8aa3bu);  // 1/ln2 rounded to fp32
     const float y = __fmul_rn(x, LOG2E);
-    const float n = rintf(y);
+    // n = rint(y) (half to even) without the conversion pipe: adding
+    // 1.5 * 2^23 rounds y to an integer in the low mantissa bits (|y| < 2^22)
+    const float MAGIC = 12582912.0f;
+    const float t = __fadd_rn(y, MAGIC);
+    const float n = __fsub_rn(t, MAGIC);
     const float f = __fsub_rn(y, n);
     float p = kb_bits_to_float(0x3aaec3ffu);             // ln2^5/5!
     p = __fmaf_rn(p, f, kb_bits_to_float(0x3c1d955bu));  // ln2^4/4!
@@ -69,7 +73,7 @@ __device__ __forceinline__ float kb_expf(float x) {
     p = __fmaf_rn(p, f, kb_bits_to_float(0x3e75fdf0u));  // ln2^2/2!
     p = __fmaf_rn(p, f, kb_bits_to_float(0x3f317218u));  // ln2
     p = __fmaf_rn(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + (int)n * (1 << 23));
+    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) {
