@@ -173,6 +173,10 @@ def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
     ok = all(np.array_equal(a, b) for a, b in zip(dp.fetch(), seqs))
     # end to end through the plan API: bitstreams from pinned host memory in,
     # tokens out, inside the timed region
+    del dp
+    warm = DecompressPlan(codec, lens, [Td] * Bd)  # allocator warm-up, untimed
+    del warm
+    torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -316,6 +320,14 @@ def main():
                 "traffic": None, "per_family": kern}
 
     # ---- end-to-end through the public API ---------------------------------
+    # a plan per step, as a caller compressing batch after batch would; the
+    # device-resident plan is released first and one untimed plan warms the
+    # allocator, so the timed steps reuse cached device and pinned blocks
+    del plan
+    p2 = CompressPlan(codec, [args.T] * args.B)
+    p2.upload(seqs)
+    p2.run()
+    p2.fetch()
     torch.cuda.synchronize()
     barrier()
     t0 = time.perf_counter()
@@ -323,6 +335,7 @@ def main():
     e3 = torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(max(1, args.steps)):
+        p2 = None
         p2 = CompressPlan(codec, [args.T] * args.B)
         p2.upload(seqs)
         p2.run()

@@ -306,9 +306,11 @@ size_t kb_step_workspace_bytes(const kb_model* model, int B);
 int kb_step_forward(kb_model* model, const int32_t* tokens, int B, float* state,
                     void* workspace, size_t workspace_bytes, uint16_t* logits,
                     float* logit_stats, void* stream);
-/* Profiling aid: a device buffer of >= 512 u64 receives, for CTA 0 of each
+/* Profiling aid: a device buffer of >= 1024 u64 receives, for CTA 0 of each
  * later kb_step_forward, %globaltimer at every grid barrier's entry (slot
- * 2e) and exit (slot 2e+1); NULL turns it off. */
+ * 2e) and exit (slot 2e+1), and per tile phase tp the times its first unit's
+ * loads were issued, landed, multiplied and stored (slots 512 + 4 tp ..);
+ * NULL turns it off. */
 int kb_step_set_trace(unsigned long long* trace);
 /* Device-side failure report of the fused step (bounded mbarrier and grid
  * barrier waits): KB_OK or KB_ERR_TIMEOUT; reset != 0 clears it. */

@@ -55,6 +55,7 @@ constexpr int SF_MAX_C = 2048;                   // row staging per group
 constexpr size_t SF_ROW_OFF = SF_A_BYTES + 2 * SF_W_BYTES + 256;
 constexpr size_t SF_SMEM = SF_ROW_OFF + 2 * (SF_MAX_C + 8) * 4 + 1024 /*align*/;
 constexpr uint32_t SF_IDESC = tc::idesc_i8(128, SF_BN);
+constexpr int SF_TRACE_TILE = 512;  // trace slots of CTA 0's first unit per tile phase
 constexpr unsigned long long SF_SPIN_NS = 2000000000ull;  // grid-barrier wait bound: 2 s
 
 // GEMMs of a layer, in weight-map order
@@ -248,10 +249,13 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
             for (int kb = 0; kb < un.nkb; ++kb)
                 tc::tma_load_2d(abuf + kb * SF_A_BLK, &p.amap[un.amap], &sb->a_full,
                                 un.k0 + kb * 128, un.mt * 128);
+            const bool tr = p.trace && blockIdx.x == 0 && first;
+            if (tr) p.trace[SF_TRACE_TILE + 4 * tp] = gtimer();
             bool ok = tc::mbar_wait(&sb->w_full[wb], st.w_uses[wb] & 1u);
             ok = tc::mbar_wait(&sb->a_full, st.a_uses & 1u) && ok;
             st.w_uses[wb]++;
             st.a_uses++;
+            if (tr) p.trace[SF_TRACE_TILE + 4 * tp + 1] = gtimer();
             if (!ok) {
                 sf_fail(p, 1);
             } else {
@@ -267,9 +271,10 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
             tc::mma_commit(&sb->mma_done);
         }
         __syncwarp();
-        first = false;
         // epilogue: warp w drains TMEM lanes 32*(w%4).. and columns 32*(w/4)..
         if (!tc::mbar_wait(&sb->mma_done, st.mma_uses & 1u)) sf_fail(p, 2);
+        if (p.trace && blockIdx.x == 0 && threadIdx.x == 0 && first)
+            p.trace[SF_TRACE_TILE + 4 * tp + 2] = gtimer();
         st.mma_uses++;
         __syncwarp();
         tc::fence_after_sync();
@@ -291,6 +296,9 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
         }
         tc::fence_before_sync();
         __syncthreads();
+        if (p.trace && blockIdx.x == 0 && threadIdx.x == 0 && first)
+            p.trace[SF_TRACE_TILE + 4 * tp + 3] = gtimer();
+        first = false;
     }
     // prefetch the weights of this CTA's first unit of the next tile phase
     if (threadIdx.x == 0 && tp + 1 < 4 * p.L) {
@@ -931,9 +939,11 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
     }
 }
 
-// Profiling aid: when trace is non-NULL (device, >= 2 * 256 u64), CTA 0 of
+// Profiling aid: when trace is non-NULL (device, >= 1024 u64), CTA 0 of
 // every later kb_step_forward records %globaltimer at each grid barrier's
-// entry (even slots) and exit (odd slots).  NULL turns it off.
+// entry (even slots) and exit (odd slots), and for its first unit of tile
+// phase tp at slots 512 + 4 tp + {loads issued, operands landed, MMAs done,
+// partials stored}.  NULL turns it off.
 extern "C" int kb_step_set_trace(unsigned long long* trace) {
     kb::g_step_trace = trace;
     return KB_OK;
