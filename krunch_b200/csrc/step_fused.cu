@@ -53,9 +53,9 @@ constexpr uint32_t SF_A_BYTES = SF_MAX_KB * SF_A_BLK;
 constexpr uint32_t SF_W_BYTES = SF_MAX_KB * SF_W_BLK;
 constexpr int SF_MAX_C = 2048;                   // row staging per group
 constexpr size_t SF_ROW_OFF = SF_A_BYTES + 2 * SF_W_BYTES + 256;
-constexpr size_t SF_SMEM = SF_ROW_OFF + 2 * (SF_MAX_C + 8) * 4 + 1024 /*align*/;
 constexpr uint32_t SF_IDESC = tc::idesc_i8(128, SF_BN);
-constexpr int SF_TRACE_TILE = 512;  // trace slots of CTA 0's first unit per tile phase
+constexpr int SF_TRACE_TILE = 512;  // + 4 tp: SM clock of CTA 0's first unit
+constexpr int SF_TRACE_CLK = 768;   // + epoch: SM clock at barrier exit  // trace slots of CTA 0's first unit per tile phase
 constexpr unsigned long long SF_SPIN_NS = 2000000000ull;  // grid-barrier wait bound: 2 s
 
 // GEMMs of a layer, in weight-map order
@@ -69,9 +69,9 @@ struct SfLayer {
     const uint16_t* wscale[G_NUM];
 };
 
-struct SfParams {
-    CUtensorMap wmap[SF_MAX_LAYERS][G_NUM];  // int8 weights, box 128 B x 64 rows
-    CUtensorMap amap[A_NUM];                 // int8 activations, box 128 B x 128 rows
+// Everything but the tensor maps; copied to shared memory at kernel start so
+// the phases read it without constant-cache misses.
+struct SfHot {
     SfLayer layer[SF_MAX_LAYERS];
     int L, B, C, F, V, conv;
     int ks[G_NUM];   // K slices per GEMM
@@ -86,6 +86,17 @@ struct SfParams {
     unsigned* bar;         // [0] arrivals, [1] abort flag; zeroed before launch
     unsigned long long* trace;  // optional: CTA 0's %globaltimer at barrier entry/exit
 };
+
+struct SfParams {
+    CUtensorMap wmap[SF_MAX_LAYERS][G_NUM];  // int8 weights, box 128 B x 64 rows
+    CUtensorMap amap[A_NUM];                 // int8 activations, box 128 B x 128 rows
+    CUtensorMap pmap[G_NUM];                 // int32 partials [slice][B][N], box 32 x 128 x 1
+    SfHot h;
+};
+
+constexpr size_t SF_HOT_OFF = SF_ROW_OFF + 2 * (SF_MAX_C + 8) * 4;
+constexpr size_t SF_SMEM = SF_HOT_OFF + sizeof(SfHot) + 1024 /*align*/;
+static_assert(SF_SMEM <= 232448, "shared memory per block");
 
 __device__ int g_step_error = 0;
 
@@ -104,7 +115,7 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
-__device__ __forceinline__ void sf_fail(const SfParams& p, int code) {
+__device__ __forceinline__ void sf_fail(const SfHot& p, int code) {
     atomicExch(&g_step_error, code);
     atomicExch(p.bar + 1, 1u);
 }
@@ -117,7 +128,7 @@ __device__ __forceinline__ unsigned long long gtimer() {
     return t;
 }
 
-__device__ bool grid_sync(const SfParams& p, SfBars* sb, unsigned epoch) {
+__device__ bool grid_sync(const SfHot& p, SfBars* sb, unsigned epoch) {
     __syncthreads();
     if (threadIdx.x == 0 && blockIdx.x == 0 && p.trace) p.trace[2 * epoch] = gtimer();
     if (threadIdx.x == 0) {
@@ -145,7 +156,10 @@ __device__ bool grid_sync(const SfParams& p, SfBars* sb, unsigned epoch) {
         }
         fence_proxy_async_global();
         sb->ok = ok;
-        if (blockIdx.x == 0 && p.trace) p.trace[2 * epoch + 1] = gtimer();
+        if (blockIdx.x == 0 && p.trace) {
+            p.trace[2 * epoch + 1] = gtimer();
+            p.trace[SF_TRACE_CLK + epoch] = clock64();
+        }
     }
     __syncthreads();
     return sb->ok != 0;
@@ -160,7 +174,7 @@ struct Job {
 };
 
 // The jobs of tile phase tp (4 per layer).
-__device__ __forceinline__ int phase_jobs(const SfParams& p, int tp, Job (&j)[3]) {
+__device__ __forceinline__ int phase_jobs(const SfHot& p, int tp, Job (&j)[3]) {
     const int C = p.C, F = p.F;
     switch (tp & 3) {
         case 0:
@@ -185,12 +199,12 @@ struct Unit {
     int g, amap, N, mt, nt, k0, nkb, ks;
 };
 
-__device__ __forceinline__ int units_of(const SfParams& p, const Job& jb) {
+__device__ __forceinline__ int units_of(const SfHot& p, const Job& jb) {
     return ((p.B + 127) / 128) * (jb.N / SF_BN) * jb.ks;
 }
 
 // Unit u of tile phase tp; false past the last unit.
-__device__ bool unit_at(const SfParams& p, int tp, int u, Unit& out) {
+__device__ bool unit_at(const SfHot& p, int tp, int u, Unit& out) {
     Job j[3];
     const int nj = phase_jobs(p, tp, j);
     for (int i = 0; i < nj; ++i) {
@@ -214,11 +228,11 @@ __device__ bool unit_at(const SfParams& p, int tp, int u, Unit& out) {
 }
 
 // thread 0: weight tile of unit `un` (layer l) into W buffer `wb`
-__device__ __forceinline__ void issue_w(const SfParams& p, SfBars* sb, unsigned char* wbuf, int wb,
+__device__ __forceinline__ void issue_w(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* wbuf, int wb,
                                         int l, const Unit& un) {
     tc::mbar_expect_tx(&sb->w_full[wb], (uint32_t)un.nkb * SF_W_BLK);
     for (int kb = 0; kb < un.nkb; ++kb)
-        tc::tma_load_2d(wbuf + kb * SF_W_BLK, &p.wmap[l][un.g], &sb->w_full[wb], un.k0 + kb * 128,
+        tc::tma_load_2d(wbuf + kb * SF_W_BLK, &P.wmap[l][un.g], &sb->w_full[wb], un.k0 + kb * 128,
                         un.nt * SF_BN);
 }
 
@@ -231,7 +245,7 @@ struct SfState {
 
 // Runs this CTA's units of tile phase tp (layer l).  The first unit's weights
 // were prefetched into buffer (tp & 1) at the end of the previous tile phase.
-__device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
+__device__ bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
                            int tp, SfState& st) {
     const int l = tp >> 2;
     const int wb = tp & 1;
@@ -243,19 +257,19 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
         Unit un;
         if (!unit_at(p, tp, u, un)) break;
         if (threadIdx.x == 0) {
-            if (!(first && st.w_pending[wb])) issue_w(p, sb, wbuf, wb, l, un);
+            if (!(first && st.w_pending[wb])) issue_w(P, p, sb, wbuf, wb, l, un);
             st.w_pending[wb] = 0;
             tc::mbar_expect_tx(&sb->a_full, (uint32_t)un.nkb * SF_A_BLK);
             for (int kb = 0; kb < un.nkb; ++kb)
-                tc::tma_load_2d(abuf + kb * SF_A_BLK, &p.amap[un.amap], &sb->a_full,
+                tc::tma_load_2d(abuf + kb * SF_A_BLK, &P.amap[un.amap], &sb->a_full,
                                 un.k0 + kb * 128, un.mt * 128);
             const bool tr = p.trace && blockIdx.x == 0 && first;
-            if (tr) p.trace[SF_TRACE_TILE + 4 * tp] = gtimer();
+            if (tr) p.trace[SF_TRACE_TILE + 4 * tp] = clock64();
             bool ok = tc::mbar_wait(&sb->w_full[wb], st.w_uses[wb] & 1u);
             ok = tc::mbar_wait(&sb->a_full, st.a_uses & 1u) && ok;
             st.w_uses[wb]++;
             st.a_uses++;
-            if (tr) p.trace[SF_TRACE_TILE + 4 * tp + 1] = gtimer();
+            if (tr) p.trace[SF_TRACE_TILE + 4 * tp + 1] = clock64();
             if (!ok) {
                 sf_fail(p, 1);
             } else {
@@ -272,32 +286,42 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
         }
         __syncwarp();
         // epilogue: warp w drains TMEM lanes 32*(w%4).. and columns 32*(w/4)..
-        if (!tc::mbar_wait(&sb->mma_done, st.mma_uses & 1u)) sf_fail(p, 2);
-        if (p.trace && blockIdx.x == 0 && threadIdx.x == 0 && first)
-            p.trace[SF_TRACE_TILE + 4 * tp + 2] = gtimer();
+        // (thread 0 waits for the MMAs; the others wait at the CTA barrier)
+        if (threadIdx.x == 0) {
+            if (!tc::mbar_wait(&sb->mma_done, st.mma_uses & 1u)) sf_fail(p, 2);
+            if (p.trace && blockIdx.x == 0 && first) p.trace[SF_TRACE_TILE + 4 * tp + 2] = clock64();
+        }
         st.mma_uses++;
         __syncwarp();
+        __syncthreads();
         tc::fence_after_sync();
         {
+            // stage the 128 x 64 int32 tile in the (now free) A buffer: two
+            // 128-row x 128-byte halves in the 128-byte swizzle, then two TMA
+            // stores into the [slice][B][N] partials (rows >= B clipped)
             const int q = warp & 3, ch = warp >> 2;
             uint32_t v[32];
             tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 32), v);
             tc::tmem_ld_wait();
-            const int row = un.mt * 128 + q * 32 + lane;
-            if (row < p.B) {
-                int4* dst = reinterpret_cast<int4*>(p.part[un.g] +
-                                                    ((int64_t)un.ks * p.B + row) * un.N +
-                                                    un.nt * SF_BN + ch * 32);
+            const int r = q * 32 + lane;
+            unsigned char* stg = abuf + ch * 16384 + r * 128;
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    dst[k] = make_int4((int)v[4 * k], (int)v[4 * k + 1], (int)v[4 * k + 2],
-                                       (int)v[4 * k + 3]);
-            }
+            for (int k = 0; k < 8; ++k)
+                *reinterpret_cast<uint4*>(stg + ((k ^ (r & 7)) << 4)) =
+                    make_uint4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
         }
         tc::fence_before_sync();
+        tc::fence_proxy_async_smem();
         __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int ch = 0; ch < 2; ++ch)
+                tc::tma_store_3d(&P.pmap[un.g], abuf + ch * 16384, un.nt * SF_BN + ch * 32,
+                                 un.mt * 128, un.ks);
+            tc::bulk_commit();
+            tc::bulk_wait_all();  // before the grid barrier and before abuf is reused
+        }
         if (p.trace && blockIdx.x == 0 && threadIdx.x == 0 && first)
-            p.trace[SF_TRACE_TILE + 4 * tp + 3] = gtimer();
+            p.trace[SF_TRACE_TILE + 4 * tp + 3] = clock64();
         first = false;
     }
     // prefetch the weights of this CTA's first unit of the next tile phase
@@ -305,7 +329,8 @@ __device__ bool tile_phase(const SfParams& p, SfBars* sb, unsigned char* smem, u
         Unit nx;
         if (unit_at(p, tp + 1, blockIdx.x, nx)) {
             const int nb = (tp + 1) & 1;
-            issue_w(p, sb, smem + SF_A_BYTES + nb * SF_W_BYTES, nb, (tp + 1) >> 2, nx);
+            issue_w(P, p, sb, smem + SF_A_BYTES + nb * SF_W_BYTES, nb, (tp + 1) >> 2, nx);
+            tc::prefetch_tmap(&P.amap[nx.amap]);
             st.w_pending[nb] = 1;
         }
     }
@@ -441,7 +466,7 @@ __device__ __forceinline__ void ln_mix_g(const Grp& g, const float (&v)[EPL / 4]
 }
 
 template <int EPL>
-__device__ __forceinline__ void ln1_mix_g(const Grp& g, const SfParams& p, int l, int b,
+__device__ __forceinline__ void ln1_mix_g(const Grp& g, const SfHot& p, int l, int b,
                                           const float (&v)[EPL / 4]) {
     const int C = p.C;
     const size_t BC = (size_t)p.B * C;
@@ -455,7 +480,7 @@ __device__ __forceinline__ void ln1_mix_g(const Grp& g, const SfParams& p, int l
 
 // embedding + LN1 of layer 0
 template <int EPL>
-__device__ void row_embed(const Grp& g, const SfParams& p, int b) {
+__device__ void row_embed(const Grp& g, const SfHot& p, int b) {
     constexpr int NE = EPL / 4;
     const int C = p.C;
     int t = p.tokens[b];
@@ -475,7 +500,7 @@ __device__ void row_embed(const Grp& g, const SfParams& p, int b) {
 
 // k, v, r -> WKV -> r*y, quantised
 template <int EPL>
-__device__ void row_wkv(const Grp& g, const SfParams& p, int l, int b) {
+__device__ void row_wkv(const Grp& g, const SfHot& p, int l, int b) {
     constexpr int NE = EPL / 4;
     const int C = p.C;
     const size_t BC = (size_t)p.B * C;
@@ -521,7 +546,7 @@ __device__ void row_wkv(const Grp& g, const SfParams& p, int l, int b) {
 
 // x += (r*y) @ Ow; LN2 + the two channel-mix outputs, quantised; ffn_xx <- LN2(x)
 template <int EPL>
-__device__ void row_att_out(const Grp& g, const SfParams& p, int l, int b) {
+__device__ void row_att_out(const Grp& g, const SfHot& p, int l, int b) {
     constexpr int NE = EPL / 4;
     const int C = p.C;
     const size_t BC = (size_t)p.B * C;
@@ -553,7 +578,7 @@ __device__ void row_att_out(const Grp& g, const SfParams& p, int l, int b) {
 // kk = relu(k)^2 quantised per row (F = 4C: EPL values per thread);
 // r2 = sigmoid(r) (fp16)
 template <int EPL>
-__device__ void row_ffn_mid(const Grp& g, const SfParams& p, int l, int b) {
+__device__ void row_ffn_mid(const Grp& g, const SfHot& p, int l, int b) {
     constexpr int NE = EPL / 4, NF = EPL;
     const int C = p.C, F = p.F;
     const SfLayer& ly = p.layer[l];
@@ -577,7 +602,7 @@ __device__ void row_ffn_mid(const Grp& g, const SfParams& p, int l, int b) {
 
 // x += r2 * (kk @ Vw); then LN1 + mix of layer l+1, or ln_out + quantisation
 template <int EPL>
-__device__ void row_ffn_out(const Grp& g, const SfParams& p, int l, int b) {
+__device__ void row_ffn_out(const Grp& g, const SfHot& p, int l, int b) {
     constexpr int NE = EPL / 4;
     const int C = p.C;
     const SfLayer& ly = p.layer[l];
@@ -611,10 +636,17 @@ __device__ void row_ffn_out(const Grp& g, const SfParams& p, int l, int b) {
 }
 
 template <int EPL>
-__global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__ SfParams p) {
+__global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__ SfParams P) {
     extern __shared__ unsigned char sf_smem_raw[];
     const uint32_t raw = tc::smem_addr(sf_smem_raw);
     unsigned char* smem = sf_smem_raw + (((raw + 1023u) & ~1023u) - raw);
+    SfHot& p = *reinterpret_cast<SfHot*>(smem + SF_HOT_OFF);
+    {
+        static_assert(sizeof(SfHot) % 4 == 0, "word copy");
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&P.h);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(&p);
+        for (int i = threadIdx.x; i < (int)(sizeof(SfHot) / 4); i += blockDim.x) dst[i] = src[i];
+    }
     SfBars* sb = reinterpret_cast<SfBars*>(smem + SF_A_BYTES + 2 * SF_W_BYTES);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -636,7 +668,7 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     if (threadIdx.x == 0) {
         Unit u0;
         if (unit_at(p, 0, blockIdx.x, u0)) {
-            issue_w(p, sb, smem + SF_A_BYTES, 0, 0, u0);
+            issue_w(P, p, sb, smem + SF_A_BYTES, 0, 0, u0);
             st.w_pending[0] = 1;
         }
     }
@@ -654,19 +686,19 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     for (int b = gw; b < p.B; b += nw) row_embed<EPL>(grp, p, b);
     ok = grid_sync(p, sb, ++epoch);
     for (int l = 0; l < p.L && ok; ++l) {
-        tile_phase(p, sb, smem, tmem, 4 * l + 0, st);
+        tile_phase(P, p, sb, smem, tmem, 4 * l + 0, st);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
         for (int b = gw; b < p.B; b += nw) row_wkv<EPL>(grp, p, l, b);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        tile_phase(p, sb, smem, tmem, 4 * l + 1, st);
+        tile_phase(P, p, sb, smem, tmem, 4 * l + 1, st);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
         for (int b = gw; b < p.B; b += nw) row_att_out<EPL>(grp, p, l, b);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        tile_phase(p, sb, smem, tmem, 4 * l + 2, st);
+        tile_phase(P, p, sb, smem, tmem, 4 * l + 2, st);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
         for (int b = gw; b < p.B; b += nw) row_ffn_mid<EPL>(grp, p, l, b);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        tile_phase(p, sb, smem, tmem, 4 * l + 3, st);
+        tile_phase(P, p, sb, smem, tmem, 4 * l + 3, st);
         if (!(ok = grid_sync(p, sb, ++epoch))) break;
         for (int b = gw; b < p.B; b += nw) row_ffn_out<EPL>(grp, p, l, b);
         if (l + 1 < p.L && !(ok = grid_sync(p, sb, ++epoch))) break;
@@ -713,6 +745,20 @@ bool map_i8(CUtensorMap* map, const void* base, int rows, int cols, int box_rows
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// int32 partial sums [slices][B][N], box 32 columns x 128 rows x 1 slice,
+// 128-byte swizzle (the staging layout)
+bool map_part(CUtensorMap* map, void* base, int N, int B, int slices) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)B, (cuuint64_t)slices};
+    cuuint64_t strides[2] = {(cuuint64_t)N * 4, (cuuint64_t)B * N * 4};
+    cuuint32_t box[3] = {32, 128, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, base, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 inline size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -827,62 +873,66 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
             c->p.reset(new (std::nothrow) SfParams());
             if (!c->p) return KB_ERR_NOMEM;
             SfParams& q = *c->p;
-            q.L = d.n_layer;
-            q.B = B;
-            q.C = d.n_embd;
-            q.F = d.n_ffn;
-            q.V = d.n_vocab;
-            q.conv = d.wkv_convention;
-            for (int g = 0; g < G_NUM; ++g) q.ks[g] = lo.ks[g];
+            q.h.L = d.n_layer;
+            q.h.B = B;
+            q.h.C = d.n_embd;
+            q.h.F = d.n_ffn;
+            q.h.V = d.n_vocab;
+            q.h.conv = d.wkv_convention;
+            for (int g = 0; g < G_NUM; ++g) q.h.ks[g] = lo.ks[g];
             for (int l = 0; l < d.n_layer; ++l) {
                 const kb_layer_desc& L = d.layers[l];
                 const void* W[G_NUM] = {L.att_kw, L.att_vw, L.att_rw, L.att_ow,
                                         L.ffn_kw, L.ffn_rw, L.ffn_vw};
                 const uint16_t* S[G_NUM] = {L.att_ks, L.att_vs, L.att_rs, L.att_os,
                                             L.ffn_ks, L.ffn_rs, L.ffn_vs};
-                const int Nn[G_NUM] = {q.C, q.C, q.C, q.C, q.F, q.C, q.C};
-                const int Kk[G_NUM] = {q.C, q.C, q.C, q.C, q.C, q.C, q.F};
+                const int Nn[G_NUM] = {q.h.C, q.h.C, q.h.C, q.h.C, q.h.F, q.h.C, q.h.C};
+                const int Kk[G_NUM] = {q.h.C, q.h.C, q.h.C, q.h.C, q.h.C, q.h.C, q.h.F};
                 for (int g = 0; g < G_NUM; ++g) {
                     if (!map_i8(&q.wmap[l][g], W[g], Nn[g], Kk[g], SF_BN))
                         return KB_ERR_UNSUPPORTED;
-                    q.layer[l].wscale[g] = S[g];
+                    q.h.layer[l].wscale[g] = S[g];
                 }
-                SfLayer& y = q.layer[l];
+                SfLayer& y = q.h.layer[l];
                 y.ln1_w = L.ln1_w; y.ln1_b = L.ln1_b; y.ln2_w = L.ln2_w; y.ln2_b = L.ln2_b;
                 y.mix_k = L.att_mix_k; y.mix_v = L.att_mix_v; y.mix_r = L.att_mix_r;
                 y.decay = L.att_decay; y.first = L.att_first;
                 y.fmix_k = L.ffn_mix_k; y.fmix_r = L.ffn_mix_r;
             }
-            q.emb = d.emb;
-            q.ln_out_w = d.ln_out_w;
-            q.ln_out_b = d.ln_out_b;
-            q.x = (uint16_t*)(base + lo.x);
-            q.kk = (uint16_t*)(base + lo.kk);
-            q.r2 = (uint16_t*)(base + lo.r2);
-            q.q_kx = (int8_t*)(base + lo.q_kx);
-            q.q_vx = (int8_t*)(base + lo.q_vx);
-            q.q_rx = (int8_t*)(base + lo.q_rx);
-            q.q_ry = (int8_t*)(base + lo.q_ry);
-            q.q_kk = (int8_t*)(base + lo.q_kk);
-            q.s_kx = (float*)(base + lo.s_kx);
-            q.s_vx = (float*)(base + lo.s_vx);
-            q.s_rx = (float*)(base + lo.s_rx);
-            q.s_ry = (float*)(base + lo.s_ry);
-            q.s_kk = (float*)(base + lo.s_kk);
-            for (int g = 0; g < G_NUM; ++g) q.part[g] = (int32_t*)(base + lo.part[g]);
-            q.bar = (unsigned*)(base + lo.bar);
-            const void* A[A_NUM] = {q.q_kx, q.q_vx, q.q_rx, q.q_ry, q.q_kk};
-            const int Ak[A_NUM] = {q.C, q.C, q.C, q.C, q.F};
+            q.h.emb = d.emb;
+            q.h.ln_out_w = d.ln_out_w;
+            q.h.ln_out_b = d.ln_out_b;
+            q.h.x = (uint16_t*)(base + lo.x);
+            q.h.kk = (uint16_t*)(base + lo.kk);
+            q.h.r2 = (uint16_t*)(base + lo.r2);
+            q.h.q_kx = (int8_t*)(base + lo.q_kx);
+            q.h.q_vx = (int8_t*)(base + lo.q_vx);
+            q.h.q_rx = (int8_t*)(base + lo.q_rx);
+            q.h.q_ry = (int8_t*)(base + lo.q_ry);
+            q.h.q_kk = (int8_t*)(base + lo.q_kk);
+            q.h.s_kx = (float*)(base + lo.s_kx);
+            q.h.s_vx = (float*)(base + lo.s_vx);
+            q.h.s_rx = (float*)(base + lo.s_rx);
+            q.h.s_ry = (float*)(base + lo.s_ry);
+            q.h.s_kk = (float*)(base + lo.s_kk);
+            for (int g = 0; g < G_NUM; ++g) q.h.part[g] = (int32_t*)(base + lo.part[g]);
+            q.h.bar = (unsigned*)(base + lo.bar);
+            const void* A[A_NUM] = {q.h.q_kx, q.h.q_vx, q.h.q_rx, q.h.q_ry, q.h.q_kk};
+            const int Ak[A_NUM] = {q.h.C, q.h.C, q.h.C, q.h.C, q.h.F};
             for (int a = 0; a < A_NUM; ++a)
                 if (!map_i8(&q.amap[a], A[a], B, Ak[a], 128)) return KB_ERR_UNSUPPORTED;
+            const int Np[G_NUM] = {q.h.C, q.h.C, q.h.C, q.h.C, q.h.F, q.h.C, q.h.C};
+            for (int g = 0; g < G_NUM; ++g)
+                if (!map_part(&q.pmap[g], q.h.part[g], Np[g], B, lo.ks[g]))
+                    return KB_ERR_UNSUPPORTED;
             m->step_cache = c;
             cache = c;
         }
         p = cache->p.get();
     }
-    p->tokens = tokens;
-    p->state = state;
-    p->trace = g_step_trace;
+    p->h.tokens = tokens;
+    p->h.state = state;
+    p->h.trace = g_step_trace;
 
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
@@ -901,7 +951,7 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
     {
         ProfScope ps(PH_STEP, st, 2.0 * B * (double)d.n_layer *
                                       (5.0 * d.n_embd * d.n_embd + 2.0 * d.n_embd * d.n_ffn));
-        cudaError_t e = cudaMemsetAsync(p->bar, 0, 2 * sizeof(unsigned), st);
+        cudaError_t e = cudaMemsetAsync(p->h.bar, 0, 2 * sizeof(unsigned), st);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             return KB_ERR_CUDA;
@@ -930,10 +980,10 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
         ProfScope ps(PH_HEAD, st, 2.0 * B * (double)d.n_vocab * d.n_embd);
         const int8_t* hw = (const int8_t*)d.head;
         if (logit_stats)
-            return launch_gemm_logits_i8(p->q_kx, d.n_embd, p->s_kx, hw, d.n_embd, d.head_scale,
+            return launch_gemm_logits_i8(p->h.q_kx, d.n_embd, p->h.s_kx, hw, d.n_embd, d.head_scale,
                                          B, d.vocab_pad, d.n_embd, logits, d.vocab_pad, d.n_vocab,
                                          logit_stats, d.vocab_pad / 32, st);
-        return launch_gemm_i8(p->q_kx, d.n_embd, p->s_kx, hw, d.n_embd, d.head_scale, B,
+        return launch_gemm_i8(p->h.q_kx, d.n_embd, p->h.s_kx, hw, d.n_embd, d.head_scale, B,
                               d.vocab_pad, d.n_embd, KB_EPI_F16, logits, d.vocab_pad, nullptr,
                               nullptr, st);
     }
@@ -943,7 +993,8 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
 // every later kb_step_forward records %globaltimer at each grid barrier's
 // entry (even slots) and exit (odd slots), and for its first unit of tile
 // phase tp at slots 512 + 4 tp + {loads issued, operands landed, MMAs done,
-// partials stored}.  NULL turns it off.
+// partials stored} and at barrier exits at 768 + epoch, as SM clock counts.
+// NULL turns it off.
 extern "C" int kb_step_set_trace(unsigned long long* trace) {
     kb::g_step_trace = trace;
     return KB_OK;
