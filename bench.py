@@ -41,7 +41,10 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "compress MB/s of input (RWKV-4-169M, 16-bit CDF, byte-exact)"
 BYTES_PER_TOKEN = 1.0
-SHAPE = dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277)
+SHAPES = {"169m": dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277),
+          # the larger-model stress case
+          "1.5b": dict(n_layer=24, n_embd=2048, n_ffn=8192, n_vocab=50277)}
+SHAPE = SHAPES["169m"]
 
 
 def peaks():
@@ -210,8 +213,12 @@ def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
 
 
 def config(args):
-    return {"workload": "configs[1] compress, packed forward, 1 GPU per rank",
-            "model": "RWKV-4-169M random-init fp16", "chunks_per_gpu": args.B,
+    name = "RWKV-4-169M" if args.model == "169m" else "RWKV-4 1.5B architecture"
+    wl = ("configs[1] compress, packed forward, 1 GPU per rank" if args.model == "169m"
+          else "configs[4] compress (1.5B stress), packed forward, 1 GPU per rank")
+    return {"workload": wl,
+            "model": f"{name} random-init {'w8a8 int8' if args.wdtype == 'i8' else 'fp16'}",
+            "chunks_per_gpu": args.B,
             "tokens_per_chunk": args.T, "cdf_bits": args.cdf_bits,
             "bytes_per_token": BYTES_PER_TOKEN, "token_dist": "Zipf(1.1) via seeded permutation",
             "global_batch": args.B * args.gpus, "seq_len": args.T,
@@ -231,11 +238,16 @@ def main():
     ap.add_argument("--ref-chunks", type=int, default=4)
     ap.add_argument("--ref-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", default="169m", choices=sorted(SHAPES))
+    ap.add_argument("--wdtype", default="f16", choices=["f16", "i8"],
+                    help="weights of the compress line (the decompress line is always w8a8)")
     ap.add_argument("--no-decompress", action="store_true",
                     help="skip the configs[2] decompress line (w8a8, B=256 x 2048 steps)")
     ap.add_argument("--dec-B", type=int, default=256)
     ap.add_argument("--dec-T", type=int, default=2048)
     args = ap.parse_args()
+    global SHAPE
+    SHAPE = SHAPES[args.model]
     if args.impl == "reference":
         return run_reference(args)
 
@@ -253,7 +265,7 @@ def main():
     dev = torch.device("cuda", kd.local_rank() % torch.cuda.device_count())
     torch.cuda.set_device(dev)
     w = random_weights(**SHAPE, seed=0)
-    model = RWKVModel(w, device=dev)
+    model = RWKVModel(w, device=dev, wdtype=args.wdtype)
     del w
     codec = Codec(model, cdf_bits=args.cdf_bits)
     toks = zipf_tokens((args.B, args.T), seed=rank)
@@ -298,6 +310,9 @@ def main():
 
     # ---- roofline of the dominant kernel family -----------------------------
     pk, pk_kind = peaks()
+    if args.wdtype == "i8":  # dense int8 runs at twice the bf16 rate on B200
+        pk = dict(pk, bf16_tflops_sustained=2 * pk["bf16_tflops_sustained"])
+        pk_kind += ", int8 peak = 2 x bf16"
     dom = max(("gemm", "head", "cdf", "wkv", "ln_mix"), key=lambda k: prof[k][0])
     kern = {}
     for k, (kms, n, work) in prof.items():
@@ -364,7 +379,7 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "MB/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.wdtype,
                 "data": "synthetic (Zipf token ids, random-init weights)",
                 "config": config(args), "tokens_per_s": tokens_all / (ms / 1e3),
                 "bits_per_token": 8.0 * comp_bytes / (args.B * args.T),

@@ -76,6 +76,192 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
     }
 }
 
+// The same LN + mix for wide rows (C >= 1536, C % 256 == 0), without
+// holding the row in registers: each warp stages its row in shared memory
+// (fp16, as stored) and sums the statistics chunk by chunk in the lane order
+// of ln_warp, so the bits are those of k_ln_mix.  The LN outputs of a strip's
+// previous row are kept in shared memory for the token shift.  Quantised
+// outputs take one more pass for the row maximum.
+constexpr int LNS_MAX_C = 2048;
+constexpr int LNS_WARPS = 4;  // 2 x 4 KB of row staging per warp
+
+__device__ __forceinline__ void unpack_chunk8(const uint4& q, float (&v)[8]) {
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 f = __half22float2(h[k]);
+        v[2 * k] = f.x;
+        v[2 * k + 1] = f.y;
+    }
+}
+__device__ __forceinline__ uint4 pack_chunk8(const float (&v)[8]) {
+    uint4 o;
+    __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+    return o;
+}
+__device__ __forceinline__ void load8f(const float* __restrict__ p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// statistics of a row held as fp16 chunks (chunk j of lane at index j*32+lane)
+__device__ __forceinline__ void ln_stats_chunks(const uint4* rowc, int C, int lane, float& mean,
+                                                float& rstd) {
+    const int nch = C / 256;
+    float s = 0.0f;
+    for (int j = 0; j < nch; ++j) {
+        float v[8];
+        unpack_chunk8(rowc[j * 32 + lane], v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+    }
+    mean = __fdiv_rn(warp_sum(s), (float)C);
+    float q = 0.0f;
+    for (int j = 0; j < nch; ++j) {
+        float v[8];
+        unpack_chunk8(rowc[j * 32 + lane], v);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float d = __fsub_rn(v[k], mean);
+            q = __fmaf_rn(d, d, q);
+        }
+    }
+    rstd = __frsqrt_rn(__fadd_rn(__fdiv_rn(warp_sum(q), (float)C), LN_EPS));
+}
+
+__device__ __forceinline__ void ln_chunk8(const float (&v)[8], float mean, float rstd,
+                                          const float (&w)[8], const float (&b)[8], float (&o)[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+        o[k] = __half2float(__float2half_rn(__fmaf_rn(__fmul_rn(__fsub_rn(v[k], mean), rstd), w[k], b[k])));
+}
+
+template <int NMIX>
+__global__ void __launch_bounds__(LNS_WARPS * 32) k_ln_mix_stream(
+    const uint16_t* __restrict__ x, int B, int T, int C, const float* __restrict__ lw,
+    const float* __restrict__ lb, MixArgs ma, const float* __restrict__ state_in,
+    float* __restrict__ state_out, uint16_t* __restrict__ xx_out, int rpw) {
+    __shared__ uint4 s_row[LNS_WARPS][LNS_MAX_C / 8];   // this row, fp16
+    __shared__ uint4 s_prev[LNS_WARPS][LNS_MAX_C / 8];  // LN of the previous row, fp16
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint4* rowc = s_row[warp];
+    uint4* prevc = s_prev[warp];
+    const int64_t rows = (int64_t)B * T;
+    const int64_t r0 = ((int64_t)blockIdx.x * LNS_WARPS + warp) * rpw;
+    const int nch = C / 256;
+    const bool quant = ma.q[0] != nullptr;
+    for (int jr = 0; jr < rpw; ++jr) {
+        const int64_t row = r0 + jr;
+        if (row >= rows) return;
+        const int b = (int)(row / T);
+        const int t = (int)(row - (int64_t)b * T);
+        float mean, rstd;
+        if (NMIX > 0 && t != 0 && jr == 0) {  // LN of the previous row into s_prev
+            for (int j = 0; j < nch; ++j)
+                rowc[j * 32 + lane] =
+                    *reinterpret_cast<const uint4*>(x + (row - 1) * C + (j * 32 + lane) * 8);
+            __syncwarp();
+            ln_stats_chunks(rowc, C, lane, mean, rstd);
+            for (int j = 0; j < nch; ++j) {
+                const int c0 = (j * 32 + lane) * 8;
+                float v[8], w[8], bb[8], o[8];
+                unpack_chunk8(rowc[j * 32 + lane], v);
+                load8f(lw + c0, w);
+                load8f(lb + c0, bb);
+                ln_chunk8(v, mean, rstd, w, bb, o);
+                prevc[j * 32 + lane] = pack_chunk8(o);
+            }
+            __syncwarp();
+        }
+        for (int j = 0; j < nch; ++j)
+            rowc[j * 32 + lane] = *reinterpret_cast<const uint4*>(x + row * C + (j * 32 + lane) * 8);
+        __syncwarp();
+        ln_stats_chunks(rowc, C, lane, mean, rstd);
+        // chunk j of cur (LN) and of the mixes
+        auto outputs = [&](int j, float (&cur)[8], float (&mk)[3][8]) {
+            const int c0 = (j * 32 + lane) * 8;
+            float v[8], w[8], bb[8];
+            unpack_chunk8(rowc[j * 32 + lane], v);
+            load8f(lw + c0, w);
+            load8f(lb + c0, bb);
+            ln_chunk8(v, mean, rstd, w, bb, cur);
+            if (NMIX == 0) return;
+            float prev[8];
+            if (t == 0) {
+                if (state_in) load8f(state_in + (int64_t)b * C + c0, prev);
+                else
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) prev[k] = 0.0f;
+            } else {
+                unpack_chunk8(prevc[j * 32 + lane], prev);
+            }
+#pragma unroll
+            for (int m = 0; m < NMIX; ++m) {
+                float mm[8];
+                load8f(ma.mix[m] + c0, mm);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    mk[m][k] = __half2float(__float2half_rn(
+                        __fmaf_rn(cur[k], mm[k], __fmul_rn(prev[k], __fsub_rn(1.0f, mm[k])))));
+            }
+        };
+        float inv[3] = {0.0f, 0.0f, 0.0f}, amax[3] = {0.0f, 0.0f, 0.0f};
+        if (quant) {
+            for (int j = 0; j < nch; ++j) {
+                float cur[8], mk[3][8];
+                outputs(j, cur, mk);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    if (NMIX == 0) amax[0] = fmaxf(amax[0], fabsf(cur[k]));
+#pragma unroll
+                    for (int m = 0; m < NMIX; ++m) amax[m] = fmaxf(amax[m], fabsf(mk[m][k]));
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < (NMIX > 0 ? NMIX : 1); ++m) {
+                amax[m] = warp_max(amax[m]);
+                inv[m] = q_inv(amax[m]);
+            }
+        }
+        for (int j = 0; j < nch; ++j) {
+            float cur[8], mk[3][8];
+            outputs(j, cur, mk);
+            const int c0 = (j * 32 + lane) * 8;
+            if (xx_out) *reinterpret_cast<uint4*>(xx_out + row * C + c0) = pack_chunk8(cur);
+            if (NMIX == 0 && quant)
+                *reinterpret_cast<uint2*>(ma.q[0] + row * C + c0) =
+                    make_uint2(pack4(q8(cur[0], inv[0]), q8(cur[1], inv[0]), q8(cur[2], inv[0]), q8(cur[3], inv[0])),
+                               pack4(q8(cur[4], inv[0]), q8(cur[5], inv[0]), q8(cur[6], inv[0]), q8(cur[7], inv[0])));
+#pragma unroll
+            for (int m = 0; m < NMIX; ++m) {
+                if (quant) {
+                    const float* a = mk[m];
+                    *reinterpret_cast<uint2*>(ma.q[m] + row * C + c0) = make_uint2(
+                        pack4(q8(a[0], inv[m]), q8(a[1], inv[m]), q8(a[2], inv[m]), q8(a[3], inv[m])),
+                        pack4(q8(a[4], inv[m]), q8(a[5], inv[m]), q8(a[6], inv[m]), q8(a[7], inv[m])));
+                } else {
+                    *reinterpret_cast<uint4*>(ma.out[m] + row * C + c0) = pack_chunk8(mk[m]);
+                }
+            }
+            if (t == T - 1 && state_out) {
+                float4* so = reinterpret_cast<float4*>(state_out + (int64_t)b * C + c0);
+                so[0] = make_float4(cur[0], cur[1], cur[2], cur[3]);
+                so[1] = make_float4(cur[4], cur[5], cur[6], cur[7]);
+            }
+            if (NMIX > 0) prevc[j * 32 + lane] = pack_chunk8(cur);  // for the next row
+        }
+        if (quant && lane == 0) {
+            if (NMIX == 0) ma.qs[0][row] = q_factor(amax[0]);
+#pragma unroll
+            for (int m = 0; m < NMIX; ++m) ma.qs[m][row] = q_factor(amax[m]);
+        }
+        __syncwarp();
+    }
+}
+
 template <int CONV>
 __global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float* __restrict__ k,
                                                 const float* __restrict__ v,
@@ -287,6 +473,16 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
     const int rpw = rows >= (int64_t)148 * LN_WARPS * 64 ? 4 : 1;
     const int blocks = (int)((rows + LN_WARPS * rpw - 1) / (LN_WARPS * rpw));
     int rc;
+    if (epl >= 48 && C % 256 == 0 && C <= LNS_MAX_C) {  // wide rows: streaming variant
+        const int sb = (int)((rows + LNS_WARPS * rpw - 1) / (LNS_WARPS * rpw));
+        switch (nmix) {
+            case 0: k_ln_mix_stream<0><<<sb, LNS_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in, state_out, xx_out, rpw); break;
+            case 2: k_ln_mix_stream<2><<<sb, LNS_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in, state_out, xx_out, rpw); break;
+            case 3: k_ln_mix_stream<3><<<sb, LNS_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in, state_out, xx_out, rpw); break;
+            default: return KB_ERR_ARG;
+        }
+        return launch_status();
+    }
     switch (nmix) {
         case 0: rc = ln_mix_epl<0>(epl, blocks, rpw, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;
         case 2: rc = ln_mix_epl<2>(epl, blocks, rpw, st, x, B, T, C, lw, lb, ma, state_in, state_out, xx_out); break;

@@ -108,3 +108,28 @@ def test_large_window_strips_match_small(torch):
     for b in (0, 37, 75):
         one, st_one = _run(torch, m, tok[b:b + 1])
         assert np.array_equal(one[0], big[b]), b
+
+
+@pytest.mark.parametrize("wdtype", ["f16", "i8"])
+def test_wide_rows_vs_oracle_and_stepped(torch, wdtype):
+    """C = 2048 (the 1.5B width) runs LayerNorm+mix in the streaming kernel:
+    logits near the oracle, packed == stepped bit for bit."""
+    from krunch_b200.model import RWKVModel
+    from oracle import rwkv
+    w = random_weights(2, 2048, 8192, 300, seed=9)
+    m = RWKVModel(w, wdtype=wdtype)
+    tok = np.random.default_rng(5).integers(0, 300, (2, 6))
+    packed, st_p = _run(torch, m, tok)
+    ref, _ = rwkv.forward(w, tok, wdtype="i8" if wdtype == "i8" else "f32")
+    d = np.abs(packed - ref)
+    if wdtype == "f16":
+        assert d.max() <= LOGIT_TOL
+    else:
+        assert d.mean() <= 2e-2 and d.max() <= 0.15
+    st = m.new_state(2)
+    steps = []
+    for t in range(6):
+        lg, st = _run(torch, m, tok[:, t:t + 1], st)
+        steps.append(lg[:, 0])
+    assert np.array_equal(np.stack(steps, 1), packed)
+    assert torch.equal(st, st_p)
