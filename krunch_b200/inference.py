@@ -41,11 +41,13 @@ FLAG_NO_CRC = 0x01  # assembled-from-parts blobs (krunch/job.py:206, cli.py:106)
 
 # model_id of the reference's real RWKV-4-Pile-169M weights (inference.py:50).
 REFERENCE_MODEL_ID = 1
-FAMILIES = {"169m": 1, "tiny": 2, "1b5": 3}
+# "pile169m": the pretrained RWKV-4-Pile-169M checkpoint from $KRUNCH_MODEL_DIR
+FAMILIES = {"169m": 1, "tiny": 2, "1b5": 3, "pile169m": 4}
 SHAPES = {
     "169m": dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277),
     "1b5": dict(n_layer=24, n_embd=2048, n_ffn=8192, n_vocab=50277),
     "tiny": dict(n_layer=2, n_embd=128, n_ffn=512, n_vocab=384),
+    "pile169m": dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277),
 }
 WDTYPES = {"f16": 0, "bf16": 1, "i8": 2}
 WKVS = {"step_ref": 0, "production": 1}
@@ -123,7 +125,15 @@ def build_model(cfg: CodecConfig, device="cuda"):
         dev = torch.device("cuda", torch.cuda.current_device())
     key = (cfg.family, cfg.seed, cfg.wkv, cfg.wdtype, str(dev))
     if key not in _MODEL_CACHE:
-        w = random_weights(**SHAPES[cfg.family], seed=cfg.seed)
+        if cfg.family == "pile169m":
+            from .weights import load_rwkv4_checkpoint, pretrained_path
+            path = pretrained_path()
+            if path is None:
+                raise RuntimeError("pretrained RWKV-4-Pile-169M weights not found: set "
+                                   "KRUNCH_MODEL_DIR to the directory holding them")
+            w = load_rwkv4_checkpoint(path)
+        else:
+            w = random_weights(**SHAPES[cfg.family], seed=cfg.seed)
         _MODEL_CACHE[key] = RWKVModel(w, device=dev, wkv=cfg.wkv, wdtype=cfg.wdtype)
     return _MODEL_CACHE[key]
 
