@@ -46,6 +46,14 @@ SHAPES = {"169m": dict(n_layer=12, n_embd=768, n_ffn=3072, n_vocab=50277),
           "1.5b": dict(n_layer=24, n_embd=2048, n_ffn=8192, n_vocab=50277)}
 SHAPE = SHAPES["169m"]
 
+# DRAM bytes (read + write) per launch of the dominant GEMM, from one ncu
+# capture of the ffn-key GEMM (k_gemm_tc<3,256,0>, M = 16384 rows: 30.0 MB
+# read + 50.0 MB written) scaled by 4 to the bench's 65536-row launches
+# (traffic grows with M).
+GEMM_TRAFFIC = 4 * (29.998336e6 + 49.994240e6)
+GEMM_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the ffn-key GEMM at "
+                     "M=16384 x4 = per 65536-row launch; algorithmic 4 x (25.2 + 4.7 + 100.7) MB")
+
 
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
@@ -332,7 +340,9 @@ def main():
                 "achieved": d["achieved"], "unit": d["unit"],
                 "peak": pk["bf16_tflops_sustained"] if d["unit"] == "TFLOP/s" else pk["hbm_gbs"],
                 "peak_kind": f"{pk_kind} (bf16 sustained / HBM copy)", "frac": d["frac"],
-                "traffic": None, "per_family": kern}
+                "traffic": GEMM_TRAFFIC if dom == "gemm" and args.model == "169m" else None,
+                "traffic_note": GEMM_TRAFFIC_NOTE if dom == "gemm" and args.model == "169m" else None,
+                "per_family": kern}
 
     # ---- end-to-end through the public API ---------------------------------
     # a plan per step, as a caller compressing batch after batch would; the
