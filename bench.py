@@ -225,7 +225,7 @@ def config(args):
     wl = ("configs[1] compress, packed forward, 1 GPU per rank" if args.model == "169m"
           else "configs[4] compress (1.5B stress), packed forward, 1 GPU per rank")
     return {"workload": wl,
-            "model": f"{name} random-init {'w8a8 int8' if args.wdtype == 'i8' else 'fp16'}",
+            "model": f"{name} random-init {dict(i8='w8a8 int8', bf16='bf16', f16='fp16')[args.wdtype]}",
             "chunks_per_gpu": args.B,
             "tokens_per_chunk": args.T, "cdf_bits": args.cdf_bits,
             "bytes_per_token": BYTES_PER_TOKEN, "token_dist": "Zipf(1.1) via seeded permutation",
@@ -247,7 +247,7 @@ def main():
     ap.add_argument("--ref-tokens", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model", default="169m", choices=sorted(SHAPES))
-    ap.add_argument("--wdtype", default="f16", choices=["f16", "i8"],
+    ap.add_argument("--wdtype", default="f16", choices=["f16", "bf16", "i8"],
                     help="weights of the compress line (the decompress line is always w8a8)")
     ap.add_argument("--no-decompress", action="store_true",
                     help="skip the configs[2] decompress line (w8a8, B=256 x 2048 steps)")

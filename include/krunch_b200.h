@@ -180,7 +180,9 @@ enum kb_epilogue {
 };
 enum kb_dtype { KB_F16 = 0, KB_BF16 = 1, KB_I8 = 2 };
 
-/* A, W: fp16 (dtype KB_F16).  resid/gate fp16 [M, ldo] (may alias out).
+/* A, W: both fp16 (dtype KB_F16) or both bf16 (KB_BF16; the relu^2
+ * epilogue then writes bf16, the others fp16 / fp32 as for fp16).
+ * resid/gate fp16 [M, ldo] (may alias out).
  * Requires N % 32 == 0, K % 64 == 0, 16-byte aligned rows and out. */
 int kb_gemm(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
             int M, int N, int K, int epilogue, void* out, int64_t ldo,

@@ -108,7 +108,7 @@ extern "C" int kb_model_create(const kb_model_desc* d, kb_model** out) {
     if (d->n_layer < 1 || C < 128 || F < 128 || d->n_vocab < 2) return KB_ERR_ARG;
     if (C % 128 || F % 128 || C > 4096) return KB_ERR_SHAPE;
     if (d->vocab_pad < d->n_vocab || d->vocab_pad % 128 || d->n_vocab > 65536) return KB_ERR_SHAPE;
-    if (d->wdtype != KB_F16 && d->wdtype != KB_I8) return KB_ERR_UNSUPPORTED;
+    if (d->wdtype != KB_F16 && d->wdtype != KB_I8 && d->wdtype != KB_BF16) return KB_ERR_UNSUPPORTED;
     const bool i8 = d->wdtype == KB_I8;
     if (i8 && !al16(d->head_scale)) return KB_ERR_ALIGN;
     if (d->wkv_convention != KB_WKV_STEP_REF && d->wkv_convention != KB_WKV_PRODUCTION)
@@ -222,10 +222,14 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
     const size_t BC = (size_t)B * C;
 
     const bool i8 = d.wdtype == KB_I8;
+    const bool bf = d.wdtype == KB_BF16;  // GEMM operands (mix outputs, r*y, relu^2) in bf16
     const double bpe = 2.0;  // fp16 bytes per activation element
     auto gemm = [&](const uint16_t* A, const void* W, int M, int Nn, int K, int epi, void* out,
                     const uint16_t* resid, const uint16_t* gate, int phase) -> int {
         ProfScope ps(phase, st, 2.0 * M * (double)Nn * K);
+        if (bf)
+            return launch_gemm_bf16(A, K, (const uint16_t*)W, K, M, Nn, K, epi, out, Nn, resid,
+                                    gate, st);
         return launch_gemm_tc(A, K, (const uint16_t*)W, K, M, Nn, K, epi, out, Nn, resid, gate, st);
     };
     auto gemm8 = [&](const int8_t* A, const float* sa, const void* W, const uint16_t* sw, int M,
@@ -251,7 +255,7 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
 
         // ---- time mix -------------------------------------------------------
         MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx},
-                   {w.q_kx, w.q_vx, w.q_rx}, {w.s_kx, w.s_vx, w.s_rx}};
+                   {w.q_kx, w.q_vx, w.q_rx}, {w.s_kx, w.s_vx, w.s_rx}, bf ? 1 : 0};
         {
             ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? 2 * bpe + 3 : 4 * bpe));
             KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
@@ -268,7 +272,7 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
         {
             ProfScope ps(PH_WKV, st, (double)R * C * 12.0);
             KB_TRY(launch_wkv(d.wkv_convention, B, T, C, w.k, w.v, w.r, L.att_decay, L.att_first,
-                              s_aa, s_bb, s_pp, w.ry, st));
+                              s_aa, s_bb, s_pp, w.ry, st, bf));
         }
         if (i8) {
             KB_TRY(quant(w.ry, C, w.q_ry, w.s_ry));
@@ -281,7 +285,7 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
 
         // ---- channel mix ----------------------------------------------------
         MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr},
-                   {w.q_kx, w.q_rx, nullptr}, {w.s_kx, w.s_rx, nullptr}};
+                   {w.q_kx, w.q_rx, nullptr}, {w.s_kx, w.s_rx, nullptr}, bf ? 1 : 0};
         {
             ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 2 : 3 * bpe));
             KB_TRY(launch_ln_mix(2, w.x, B, T, C, L.ln2_w, L.ln2_b, mf, s_ffn, w.xx_ffn, nullptr, st));
@@ -300,7 +304,7 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
             return launch_status();
     }
     MixArgs none{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr},
-                 {w.q_kx, nullptr, nullptr}, {w.s_kx, nullptr, nullptr}};
+                 {w.q_kx, nullptr, nullptr}, {w.s_kx, nullptr, nullptr}, bf ? 1 : 0};
     {
         ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 1 : 2 * bpe));
         KB_TRY(launch_ln_mix(0, w.x, B, T, C, d.ln_out_w, d.ln_out_b, none, nullptr, nullptr,
@@ -317,6 +321,14 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
             else
                 KB_TRY(launch_gemm_i8(w.q_kx, C, w.s_kx, hw, C, d.head_scale, R, d.vocab_pad, C,
                                       KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));
+        } else if (bf) {
+            if (logit_stats)
+                KB_TRY(launch_gemm_logits_bf16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad,
+                                               C, logits, d.vocab_pad, d.n_vocab, logit_stats,
+                                               d.vocab_pad / 32, st));
+            else
+                KB_TRY(launch_gemm_bf16(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
+                                        KB_EPI_F16, logits, d.vocab_pad, nullptr, nullptr, st));
         } else if (logit_stats) {
             KB_TRY(launch_gemm_logits(w.kx, C, (const uint16_t*)d.head, C, R, d.vocab_pad, C,
                                       logits, d.vocab_pad, d.n_vocab, logit_stats,

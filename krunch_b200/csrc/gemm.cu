@@ -15,13 +15,17 @@ extern "C" int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* 
     if (epilogue < KB_EPI_F32 || epilogue > KB_EPI_GATE_RESID) return KB_ERR_ARG;
     if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256)
         return KB_ERR_ARG;
-    if (dtype != KB_F16) return KB_ERR_UNSUPPORTED;
+    if (dtype != KB_F16 && dtype != KB_BF16) return KB_ERR_UNSUPPORTED;
     if (N % 32 || K % 64) return KB_ERR_SHAPE;
     if ((epilogue == KB_EPI_RESID || epilogue == KB_EPI_GATE_RESID) && !resid) return KB_ERR_ARG;
     if (epilogue == KB_EPI_GATE_RESID && !gate) return KB_ERR_ARG;
     if (!aligned16(A) || !aligned16(W) || (lda % 8) || (ldw % 8) || lda < K || ldw < K ||
         ldo < N || (ldo % 8) || !aligned16(out))
         return KB_ERR_ALIGN;
+    if (dtype == KB_BF16)
+        return launch_gemm_bf16(reinterpret_cast<const uint16_t*>(A), lda,
+                                reinterpret_cast<const uint16_t*>(W), ldw, M, N, K, epilogue, out,
+                                ldo, resid, gate, as_stream(stream), tile_n);
     return launch_gemm_tc(reinterpret_cast<const uint16_t*>(A), lda,
                           reinterpret_cast<const uint16_t*>(W), ldw, M, N, K, epilogue, out, ldo,
                           resid, gate, as_stream(stream), tile_n);

@@ -37,7 +37,9 @@ constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 // Tile width BN in {256, 128, 64, 32}: 256 for large M; narrower tiles give
 // a small-M launch (the decoder's B rows) more CTAs.  The K walk of an output
 // element is the same for every BN.
-enum { TC_F16 = 0, TC_I8 = 1 };
+// operand kinds: fp16, int8 (w8a8), bf16 (KB_BF16 model: bf16 weights and
+// GEMM inputs; the kernel's tensor maps move 2-byte elements either way)
+enum { TC_F16 = 0, TC_I8 = 1, TC_BF16 = 2 };
 
 template <int BN, int KIND>
 struct TcCfg {
@@ -53,7 +55,7 @@ struct TcCfg {
                                    1024 /*align*/ + 256 /*bars*/;
     static_assert(SMEM <= 232448, "shared memory per block");
     static constexpr uint32_t IDESC =
-        KIND == TC_I8 ? tc::idesc_i8(TC_BM, BN) : tc::idesc_f16(TC_BM, BN, false);
+        KIND == TC_I8 ? tc::idesc_i8(TC_BM, BN) : tc::idesc_f16(TC_BM, BN, KIND == TC_BF16);
 };
 
 // Launch parameters of one GEMM (a __grid_constant__ kernel argument).
@@ -154,8 +156,9 @@ __device__ __forceinline__ void load_tile_rows(const uint16_t* src, int64_t ld, 
 }
 
 // Epilogue values of 32 consecutive columns of one row as 16 words of fp16
-// pairs (non-F32 epilogues); rv / gv: the row's residual / gate values.
-template <int EPI>
+// pairs (bf16 pairs when OUT_BF; non-F32 epilogues); rv / gv: the row's
+// residual / gate values.
+template <int EPI, bool OUT_BF = false>
 __device__ __forceinline__ void tc_epi_pack(const uint32_t (&acc)[32], const uint4 (&rv)[4],
                                             const uint4 (&gv)[4], uint32_t (&w)[16]) {
 #pragma unroll
@@ -182,8 +185,13 @@ __device__ __forceinline__ void tc_epi_pack(const uint32_t (&acc)[32], const uin
                 y0 = epi_gate_resid(g0, y0, __low2float(rr));
                 y1 = epi_gate_resid(g1, y1, __high2float(rr));
             }
-            const __half2 p = __floats2half2_rn(y0, y1);
-            w[4 * j + h] = *reinterpret_cast<const uint32_t*>(&p);
+            if (OUT_BF) {
+                const __nv_bfloat162 p = __floats2bfloat162_rn(y0, y1);
+                w[4 * j + h] = *reinterpret_cast<const uint32_t*>(&p);
+            } else {
+                const __half2 p = __floats2half2_rn(y0, y1);
+                w[4 * j + h] = *reinterpret_cast<const uint32_t*>(&p);
+            }
         }
     }
 }
@@ -430,7 +438,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
                             load_tile_rows(args.resid, ldo, m0 + q * 32, col0, M, st, lane, rv);
                         if (EPI == KB_EPI_GATE_RESID)
                             load_tile_rows(args.gate, ldo, m0 + q * 32, col0, M, st, lane, gv);
-                        tc_epi_pack<EPI>(v, rv, gv, w);
+                        // a bf16 model's relu(k)^2 is the next GEMM's bf16 operand
+                        tc_epi_pack<EPI, KIND == TC_BF16 && EPI == KB_EPI_RELU_SQ>(v, rv, gv, w);
                         stage_and_store(st, lane, w, &mapO, col0, m0 + q * 32);
                     }
                 }
@@ -586,6 +595,24 @@ int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ld
     if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
     const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, nullptr, nullptr};
     return launch_epi<TC_F16>(A, lda, W, ldw, epi, args, st, bn);
+}
+
+int launch_gemm_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M,
+                     int N, int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
+                     const uint16_t* gate, cudaStream_t st, int bn) {
+    if (M == 0) return KB_OK;
+    if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, nullptr, nullptr};
+    return launch_epi<TC_BF16>(A, lda, W, ldw, epi, args, st, bn);
+}
+
+int launch_gemm_logits_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw,
+                            int M, int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
+                            int stats_stride, cudaStream_t st) {
+    if (M == 0) return KB_OK;
+    const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
+                      stats_stride, nullptr, nullptr};
+    return launch_epi<TC_BF16>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
 }
 
 int launch_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t* W,

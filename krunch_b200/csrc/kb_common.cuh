@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -81,6 +82,9 @@ __device__ __forceinline__ float h2f(uint16_t h) {
 }
 __device__ __forceinline__ uint16_t f2h(float f) {
     return __half_as_ushort(__float2half_rn(f));
+}
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
 }  // namespace kb

@@ -96,6 +96,24 @@ __device__ __forceinline__ void ln_warp(const float (&v)[EPL], int C, int lane,
     }
 }
 
+// bf16 rows (the GEMM operands of a KB_BF16 model), same layout as fp16
+template <int EPL>
+__device__ __forceinline__ void store_row_bf16(uint16_t* __restrict__ dst, int lane, const float (&v)[EPL]) {
+    if (RowIdx<EPL>::VEC) {
+#pragma unroll
+        for (int j = 0; j < EPL / 8; ++j) {
+            uint4 q;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&q);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[j * 8 + 2 * k], v[j * 8 + 2 * k + 1]);
+            reinterpret_cast<uint4*>(dst)[j * 32 + lane] = q;
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) dst[e * 32 + lane] = f2bf(v[e]);
+    }
+}
+
 template <int EPL>
 __device__ __forceinline__ void store_row_f16(uint16_t* __restrict__ dst, int lane, const float (&v)[EPL]) {
     if (RowIdx<EPL>::VEC) {

@@ -54,7 +54,10 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
             }
         }
         ln_warp<EPL>(v, C, lane, lw, lb, cur);
-        if (xx_out) store_row_f16<EPL>(xx_out + row * C, lane, cur);
+        if (xx_out) {
+            if (ma.bf16) store_row_bf16<EPL>(xx_out + row * C, lane, cur);
+            else store_row_f16<EPL>(xx_out + row * C, lane, cur);
+        }
         if (NMIX == 0 && ma.q[0]) store_row_q<EPL>(ma.q[0] + row * C, ma.qs[0] + row, lane, cur);
 #pragma unroll
         for (int m = 0; m < NMIX; ++m) {
@@ -65,6 +68,8 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
                 mk[e] = __fmaf_rn(cur[e], mk[e], __fmul_rn(prev[e], __fsub_rn(1.0f, mk[e])));
             if (ma.q[m])
                 store_row_q<EPL>(ma.q[m] + row * C, ma.qs[m] + row, lane, mk);
+            else if (ma.bf16)
+                store_row_bf16<EPL>(ma.out[m] + row * C, lane, mk);
             else
                 store_row_f16<EPL>(ma.out[m] + row * C, lane, mk);
         }
@@ -99,6 +104,13 @@ __device__ __forceinline__ uint4 pack_chunk8(const float (&v)[8]) {
     __half2* h = reinterpret_cast<__half2*>(&o);
 #pragma unroll
     for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+    return o;
+}
+__device__ __forceinline__ uint4 pack_chunk8_bf(const float (&v)[8]) {
+    uint4 o;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
     return o;
 }
 __device__ __forceinline__ void load8f(const float* __restrict__ p, float (&v)[8]) {
@@ -230,7 +242,9 @@ __global__ void __launch_bounds__(LNS_WARPS * 32) k_ln_mix_stream(
             float cur[8], mk[3][8];
             outputs(j, cur, mk);
             const int c0 = (j * 32 + lane) * 8;
-            if (xx_out) *reinterpret_cast<uint4*>(xx_out + row * C + c0) = pack_chunk8(cur);
+            if (xx_out)
+                *reinterpret_cast<uint4*>(xx_out + row * C + c0) =
+                    ma.bf16 ? pack_chunk8_bf(cur) : pack_chunk8(cur);
             if (NMIX == 0 && quant)
                 *reinterpret_cast<uint2*>(ma.q[0] + row * C + c0) =
                     make_uint2(pack4(q8(cur[0], inv[0]), q8(cur[1], inv[0]), q8(cur[2], inv[0]), q8(cur[3], inv[0])),
@@ -243,7 +257,8 @@ __global__ void __launch_bounds__(LNS_WARPS * 32) k_ln_mix_stream(
                         pack4(q8(a[0], inv[m]), q8(a[1], inv[m]), q8(a[2], inv[m]), q8(a[3], inv[m])),
                         pack4(q8(a[4], inv[m]), q8(a[5], inv[m]), q8(a[6], inv[m]), q8(a[7], inv[m])));
                 } else {
-                    *reinterpret_cast<uint4*>(ma.out[m] + row * C + c0) = pack_chunk8(mk[m]);
+                    *reinterpret_cast<uint4*>(ma.out[m] + row * C + c0) =
+                        ma.bf16 ? pack_chunk8_bf(mk[m]) : pack_chunk8(mk[m]);
                 }
             }
             if (t == T - 1 && state_out) {
@@ -262,7 +277,7 @@ __global__ void __launch_bounds__(LNS_WARPS * 32) k_ln_mix_stream(
     }
 }
 
-template <int CONV>
+template <int CONV, bool BF>
 __global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float* __restrict__ k,
                                                 const float* __restrict__ v,
                                                 const uint16_t* __restrict__ r,
@@ -309,7 +324,8 @@ __global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float
 #pragma unroll
         for (int j = 0; j < WKV_BLK; ++j) {
             const float y = wkv_step<CONV>(aa, bb, pp, kb[j], vb[j], u, dec);
-            op[(int64_t)j * C] = f2h(__fmul_rn(h2f(rb[j]), y));
+            const float o = __fmul_rn(h2f(rb[j]), y);
+            op[(int64_t)j * C] = BF ? f2bf(o) : f2h(o);
         }
 #pragma unroll
         for (int j = 0; j < WKV_BLK; ++j) {
@@ -325,7 +341,8 @@ __global__ void __launch_bounds__(128, 4) k_wkv(int B, int T, int C, const float
     int t0 = nblk * WKV_BLK;
     for (; t0 < T; ++t0) {
         const float y = wkv_step<CONV>(aa, bb, pp, __ldg(kp), __ldg(vp), u, dec);
-        *op = f2h(__fmul_rn(h2f(__ldg(rp)), y));
+        const float o = __fmul_rn(h2f(__ldg(rp)), y);
+        *op = BF ? f2bf(o) : f2h(o);
         kp += C;
         vp += C;
         rp += C;
@@ -495,13 +512,19 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
 
 int launch_wkv(int conv, int B, int T, int C, const float* k, const float* v, const uint16_t* r,
                const float* decay, const float* first, float* aa, float* bb, float* pp,
-               uint16_t* ry, cudaStream_t st) {
+               uint16_t* ry, cudaStream_t st, bool ry_bf16) {
     const int n = B * C;
     const int grid = (n + 127) / 128;
-    if (conv == KB_WKV_STEP_REF)
-        k_wkv<KB_WKV_STEP_REF><<<grid, 128, 0, st>>>(B, T, C, k, v, r, decay, first, aa, bb, pp, ry);
-    else
-        k_wkv<KB_WKV_PRODUCTION><<<grid, 128, 0, st>>>(B, T, C, k, v, r, decay, first, aa, bb, pp, ry);
+#define KB_WKV(CV, BFV) \
+    k_wkv<CV, BFV><<<grid, 128, 0, st>>>(B, T, C, k, v, r, decay, first, aa, bb, pp, ry)
+    if (conv == KB_WKV_STEP_REF) {
+        if (ry_bf16) KB_WKV(KB_WKV_STEP_REF, true);
+        else KB_WKV(KB_WKV_STEP_REF, false);
+    } else {
+        if (ry_bf16) KB_WKV(KB_WKV_PRODUCTION, true);
+        else KB_WKV(KB_WKV_PRODUCTION, false);
+    }
+#undef KB_WKV
     return launch_status();
 }
 

@@ -12,6 +12,7 @@ struct MixArgs {
     uint16_t* out[3];     // fp16 [rows, C] outputs
     int8_t* q[3];         // w8a8: int8 [rows, C] outputs instead (quant.cuh) ...
     float* qs[3];         // ... with their per-row dequantisation factors
+    int bf16;             // out[] (and xx_out) in bf16 instead of fp16 (KB_BF16 model)
 };
 
 int launch_embed(const int32_t* tok, int64_t rows, int V, int C, const uint16_t* emb, uint16_t* x,
@@ -19,9 +20,10 @@ int launch_embed(const int32_t* tok, int64_t rows, int V, int C, const uint16_t*
 int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float* lw,
                   const float* lb, const MixArgs& ma, const float* state_in, float* state_out,
                   uint16_t* xx_out, cudaStream_t st);
+// ry in fp16, or bf16 when ry_bf16 (the GEMM operand of a KB_BF16 model)
 int launch_wkv(int conv, int B, int T, int C, const float* k, const float* v, const uint16_t* r,
                const float* decay, const float* first, float* aa, float* bb, float* pp,
-               uint16_t* ry, cudaStream_t st);
+               uint16_t* ry, cudaStream_t st, bool ry_bf16 = false);
 int launch_state_init(float* st, int L, int B, int C, cudaStream_t s);
 
 // out[M,N] = epi(A[M,K] @ W[N,K]^T); see kb_gemm in the public header.
@@ -48,6 +50,14 @@ int launch_gemm_logits_i8(const int8_t* A, int64_t lda, const float* a_scale, co
                           int64_t ldw, const uint16_t* w_scale, int M, int N, int K,
                           uint16_t* out, int64_t ldo, int V, float* stats, int stats_stride,
                           cudaStream_t st);
+// bf16 A and W (KB_BF16 model); outputs fp16 except relu^2 (bf16: the next
+// GEMM's operand) and fp32
+int launch_gemm_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw, int M,
+                     int N, int K, int epi, void* out, int64_t ldo, const uint16_t* resid,
+                     const uint16_t* gate, cudaStream_t st, int tile_n = 0);
+int launch_gemm_logits_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw,
+                            int M, int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
+                            int stats_stride, cudaStream_t st);
 // Row-wise symmetric int8 quantisation of fp16 [R, K] (quant.cuh).
 int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, cudaStream_t st);
 // Device-side error code of the tcgen05 kernels (0 = none); optionally reset.

@@ -5,7 +5,9 @@ Weights arrive in the reference's ``model.w`` layout (matrices [in, out],
 time_decay as the raw log-decay of rwkv4_step_ref.py:89) and are stored on
 the device K-major ([out, in], fp16) for the GEMMs.
 
-``wdtype="i8"`` is the w8a8 model: every matrix (head included) quantised
+``wdtype="bf16"`` keeps every matrix in bf16 and feeds the GEMMs bf16
+inputs (the reference's KRUNCH_BF16 route, krunch_ac/cuda/layer_cpp.cpp:
+224-241: activations otherwise fp16).  ``wdtype="i8"`` is the w8a8 model: every matrix (head included) quantised
 per output channel to int8 with fp16 factors (kb_quantize_weight), the GEMM
 inputs quantised per row at run time.
 """
@@ -45,7 +47,7 @@ class RWKVModel:
     """Device-resident RWKV-4 with a kb_model handle."""
 
     def __init__(self, w: dict, device="cuda", wkv: str = "step_ref", wdtype: str = "f16"):
-        if wdtype not in ("f16", "i8"):
+        if wdtype not in ("f16", "bf16", "i8"):
             raise ValueError(f"unknown weight dtype {wdtype!r}")
         if wkv not in ("step_ref", "production"):
             raise ValueError(f"unknown WKV convention {wkv!r}")
@@ -75,8 +77,12 @@ class RWKVModel:
             self._keep += [q, sc]
             return q, sc
 
-        def kmajor(a):  # [in, out] -> fp16 [out, in]  (int8 + scales for i8)
+        def kmajor(a):  # [in, out] -> fp16 [out, in]  (int8 + scales for i8, bf16 for bf16)
             t = torch.as_tensor(np.asarray(a, dtype=np.float32)).to(dev)
+            if wdtype == "bf16":
+                t = t.t().contiguous().to(torch.bfloat16)
+                self._keep.append(t)
+                return t, None
             t = t.t().contiguous().to(torch.float16)
             if i8:
                 return quantize(t)
@@ -116,8 +122,9 @@ class RWKVModel:
             mat(d, "ffn_v", w[ffn + "value.weight"])
             mat(d, "ffn_r", w[ffn + "receptance.weight"])
         Vp = self.spec.vocab_pad
-        head = torch.zeros((Vp, Cm), dtype=torch.float16, device=dev)
-        head[:V] = torch.as_tensor(np.asarray(w["head.weight"], np.float32)).to(dev).t().half()
+        hdt = torch.bfloat16 if wdtype == "bf16" else torch.float16
+        head = torch.zeros((Vp, Cm), dtype=hdt, device=dev)
+        head[:V] = torch.as_tensor(np.asarray(w["head.weight"], np.float32)).to(dev).t().to(hdt)
         self.head_scale = None
         if i8:
             head, self.head_scale = quantize(head)
@@ -128,7 +135,7 @@ class RWKVModel:
         desc = N.ModelDesc()
         desc.n_layer, desc.n_embd, desc.n_ffn, desc.n_vocab = L, Cm, F, V
         desc.vocab_pad = Vp
-        desc.wdtype = N.KB_I8 if i8 else N.KB_F16
+        desc.wdtype = {"f16": N.KB_F16, "bf16": N.KB_BF16, "i8": N.KB_I8}[wdtype]
         desc.wkv_convention = N.KB_WKV_STEP_REF if wkv == "step_ref" else N.KB_WKV_PRODUCTION
         desc.emb = self.emb.data_ptr()
         desc.ln_out_w = f32(w["ln_out.weight"]).data_ptr()

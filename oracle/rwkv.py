@@ -78,6 +78,13 @@ def quantize_rows(x: np.ndarray):
     return q, (amax / np.float32(127)).astype(np.float32)
 
 
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bf16 (ties to even), returned as float32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
 def _mm8(x: np.ndarray, Wq) -> np.ndarray:
     """w8a8 product: exact integer accumulation, then (acc * sa) * sw."""
     q, s = Wq
@@ -92,12 +99,22 @@ def forward(w: dict, tokens: np.ndarray, state: list[np.ndarray] | None = None,
             wkv: str = "step_ref", wdtype: str = "f32") -> tuple[np.ndarray, list[np.ndarray]]:
     """tokens int [B, T] -> (logits fp32 [B, T, V], new state).
 
-    wdtype "i8" runs the w8a8 model: every matrix product through _mm8, and
+    wdtype "bf16" rounds every matrix and every GEMM input to bf16 (the
+    device's KB_BF16 model); wdtype "i8" runs the w8a8 model: every matrix
+    product through _mm8; in both,
     the activations the device keeps in fp16 (embedding, residual stream,
     LayerNorm outputs, sigmoid gates) rounded to fp16 where the device rounds
     them, so that the per-row quantisation sees the device's values."""
-    h = (lambda a: a.astype(np.float16).astype(np.float32)) if wdtype == "i8" else (lambda a: a)
-    if wdtype == "i8":
+    h = ((lambda a: a.astype(np.float16).astype(np.float32)) if wdtype in ("i8", "bf16")
+         else (lambda a: a))
+    if wdtype == "bf16":
+        bcache = {}
+
+        def mm(x, name):
+            if name not in bcache:
+                bcache[name] = bf16_round(w[name])
+            return _mm(bf16_round(x), bcache[name])
+    elif wdtype == "i8":
         qcache = {}
 
         def mm(x, name):
