@@ -10,7 +10,7 @@ import ctypes as C
 import os
 from pathlib import Path
 
-_LIB_PATH = Path(__file__).resolve().parent / "libkrunch_b200.so"
+_LIB_PATH = Path(os.environ.get("KRUNCH_B200_LIB", "") or Path(__file__).resolve().parent / "libkrunch_b200.so")  # override: another build of the library
 
 KB_OK = 0
 KB_ERR_TOO_LARGE = -9

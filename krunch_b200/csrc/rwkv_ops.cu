@@ -89,6 +89,9 @@ __global__ void __launch_bounds__(LN_WARPS * 32) k_ln_mix(const uint16_t* __rest
 // outputs take one more pass for the row maximum.
 constexpr int LNS_MAX_C = 2048;
 constexpr int LNS_WARPS = 4;  // 2 x 4 KB of row staging per warp
+#ifndef LNS_MIN_EPL
+#define LNS_MIN_EPL 48
+#endif
 
 __device__ __forceinline__ void unpack_chunk8(const uint4& q, float (&v)[8]) {
     const __half2* h = reinterpret_cast<const __half2*>(&q);
@@ -490,7 +493,7 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
     const int rpw = rows >= (int64_t)148 * LN_WARPS * 64 ? 4 : 1;
     const int blocks = (int)((rows + LN_WARPS * rpw - 1) / (LN_WARPS * rpw));
     int rc;
-    if (epl >= 48 && C % 256 == 0 && C <= LNS_MAX_C) {  // wide rows: streaming variant
+    if (epl >= LNS_MIN_EPL && C % 256 == 0 && C <= LNS_MAX_C) {  // staged variant
         const int sb = (int)((rows + LNS_WARPS * rpw - 1) / (LNS_WARPS * rpw));
         switch (nmix) {
             case 0: k_ln_mix_stream<0><<<sb, LNS_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in, state_out, xx_out, rpw); break;
