@@ -314,6 +314,12 @@ int kb_step_forward(kb_model* model, const int32_t* tokens, int B, float* state,
  * loads were issued, landed, multiplied and stored (slots 512 + 4 tp ..);
  * NULL turns it off. */
 int kb_step_set_trace(unsigned long long* trace);
+/* Failure-detection test hook of the fused step: withhold != 0 makes CTA 0
+ * skip its arrival at the first grid barrier of later calls, so every CTA's
+ * bounded wait (spin_ns; 0 = the default 2 s) expires and the launch unwinds
+ * with KB_ERR_TIMEOUT in kb_step_error_status; no GPU fault is involved.
+ * (0, 0) restores normal operation. */
+int kb_step_set_fault(int withhold, long long spin_ns);
 /* Device-side failure report of the fused step (bounded mbarrier and grid
  * barrier waits): KB_OK or KB_ERR_TIMEOUT; reset != 0 clears it. */
 int kb_step_error_status(int reset);

@@ -14,6 +14,7 @@ _LIB_PATH = Path(os.environ.get("KRUNCH_B200_LIB", "") or Path(__file__).resolve
 
 KB_OK = 0
 KB_ERR_TOO_LARGE = -9
+KB_ERR_TIMEOUT = -5
 KB_NOALLOC_SCRATCH_BYTES = 8 << 20
 KB_CDF_COUNTS, KB_CDF_CDF, KB_CDF_LOHI = 0, 1, 2
 KB_EPI_F32, KB_EPI_F16, KB_EPI_SIGMOID, KB_EPI_RELU_SQ, KB_EPI_RESID, KB_EPI_GATE_RESID = range(6)
@@ -65,6 +66,7 @@ SIGNATURES = {
     "kb_step_forward": (i32, [vp, vp, i32, vp, vp, sz, vp, vp, vp]),
     "kb_step_error_status": (i32, [i32]),
     "kb_step_set_trace": (i32, [vp]),
+    "kb_step_set_fault": (i32, [i32, i64]),
     "kb_gemm_i8": (i32, [vp, i64, vp, vp, i64, vp, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),
     "kb_quantize_weight": (i32, [vp, i32, i32, vp, vp, vp]),
     "kb_quantize_rows": (i32, [vp, i32, i32, vp, vp, vp]),

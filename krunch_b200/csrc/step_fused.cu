@@ -85,6 +85,8 @@ struct SfHot {
     int32_t* part[G_NUM];  // [ks][B][N]
     unsigned* bar;         // [0] arrivals, [1] abort flag; zeroed before launch
     unsigned long long* trace;  // optional: CTA 0's %globaltimer at barrier entry/exit
+    unsigned long long spin_ns; // grid-barrier wait bound
+    int withhold_arrival;       // test: CTA 0 does not arrive at the first barrier
 };
 
 struct SfParams {
@@ -136,7 +138,8 @@ __device__ bool grid_sync(const SfHot& p, SfBars* sb, unsigned epoch) {
         // __syncthreads above) become visible with the arrival; the proxy
         // fences order them with the TMA reads of the next tile phase
         fence_proxy_async_global();
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+        if (!(p.withhold_arrival && epoch == 1 && blockIdx.x == 0))
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
         const unsigned target = epoch * gridDim.x;
         int ok = 1;
         const unsigned long long t0 = gtimer();
@@ -147,7 +150,7 @@ __device__ bool grid_sync(const SfHot& p, SfBars* sb, unsigned epoch) {
                     ok = 0;
                     break;
                 }
-                if (gtimer() - t0 > SF_SPIN_NS) {
+                if (gtimer() - t0 > p.spin_ns) {
                     sf_fail(p, 5);
                     ok = 0;
                     break;
@@ -826,6 +829,11 @@ Layout make_layout(const kb_model_desc& d, int B, int grid) {
 }
 
 unsigned long long* g_step_trace = nullptr;
+struct StepFault {
+    unsigned long long spin_ns = 0;
+    int withhold = 0;
+};
+StepFault g_step_fault;
 
 struct StepCache {
     const void* ws = nullptr;
@@ -933,6 +941,8 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
     p->h.tokens = tokens;
     p->h.state = state;
     p->h.trace = g_step_trace;
+    p->h.spin_ns = g_step_fault.spin_ns ? g_step_fault.spin_ns : SF_SPIN_NS;
+    p->h.withhold_arrival = g_step_fault.withhold;
 
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
@@ -997,6 +1007,18 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
 // NULL turns it off.
 extern "C" int kb_step_set_trace(unsigned long long* trace) {
     kb::g_step_trace = trace;
+    return KB_OK;
+}
+
+// Failure-detection test hook: with withhold != 0, CTA 0 of every later
+// kb_step_forward skips its arrival at the first grid barrier, so every CTA's
+// bounded wait expires (after spin_ns, default 2 s when 0): the step aborts
+// cleanly and kb_step_error_status reports KB_ERR_TIMEOUT.  (0, 0) restores
+// normal operation.
+extern "C" int kb_step_set_fault(int withhold, long long spin_ns) {
+    if (spin_ns < 0) return KB_ERR_ARG;
+    kb::g_step_fault.withhold = withhold ? 1 : 0;
+    kb::g_step_fault.spin_ns = (unsigned long long)spin_ns;
     return KB_OK;
 }
 

@@ -193,3 +193,34 @@ def test_fused_step_matches_window_forward(torch, shape, B):
         assert torch.equal(la, lb), step
         assert torch.equal(sa, sb), step
         assert torch.equal(st_a, st_b), step
+
+
+def test_fused_step_bounded_wait_reports_timeout(torch):
+    """Failure detection without a GPU fault: one CTA withholds its arrival at
+    a grid barrier, every bounded wait expires (1 ms), the launch unwinds and
+    kb_step_error_status reports KB_ERR_TIMEOUT; the context stays usable and
+    the next step is bit-exact again."""
+    from krunch_b200 import _native as N
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=2), wdtype="i8")
+    B = 4
+    tok = torch.from_numpy(np.arange(B, dtype=np.int32)).cuda()
+    st = m.new_state(B)
+    ws = m.new_step_workspace(B)
+    lg, ss = m.new_logits(B, 1), m.new_stats(B, 1)
+    N.call("kb_step_error_status", 1)
+    N.call("kb_step_set_fault", 1, 1_000_000)
+    try:
+        m.step_forward(tok, st, ws, lg, ss)
+        torch.cuda.synchronize()
+    finally:
+        N.call("kb_step_set_fault", 0, 0)
+    assert N.load().kb_step_error_status(1) == N.KB_ERR_TIMEOUT
+    assert N.load().kb_step_error_status(0) == N.KB_OK  # reset
+    # usable afterwards: the fused step equals the window forward again
+    st_a, st_b = m.new_state(B), m.new_state(B)
+    la, lb = m.new_logits(B, 1), m.new_logits(B, 1)
+    m.forward_window(tok.view(B, 1), st_a, m.new_workspace(B, 1), la)
+    m.step_forward(tok, st_b, ws, lb)
+    torch.cuda.synchronize()
+    assert torch.equal(la, lb) and torch.equal(st_a, st_b)
