@@ -55,7 +55,7 @@ constexpr int SF_MAX_C = 2048;                   // row staging per group
 constexpr size_t SF_ROW_OFF = SF_A_BYTES + 2 * SF_W_BYTES + 256;
 constexpr uint32_t SF_IDESC = tc::idesc_i8(128, SF_BN);
 constexpr int SF_TRACE_TILE = 512;  // + 4 tp: SM clock of CTA 0's first unit
-constexpr int SF_TRACE_CLK = 768;   // + epoch: SM clock at barrier exit  // trace slots of CTA 0's first unit per tile phase
+constexpr int SF_TRACE_CLK = 768;   // + epoch: SM clock at barrier exit
 constexpr unsigned long long SF_SPIN_NS = 2000000000ull;  // grid-barrier wait bound: 2 s
 
 // GEMMs of a layer, in weight-map order
