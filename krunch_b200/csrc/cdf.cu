@@ -82,6 +82,30 @@ __device__ __forceinline__ int block_sum_i(int v, CdfRed& r) {
     return x;
 }
 
+// Two integer sums in one reduction (integer addition: any order, same value).
+__device__ __forceinline__ void block_sum_i2(int& a, int& b, CdfRed& r) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, off);
+        b += __shfl_xor_sync(0xffffffffu, b, off);
+    }
+    if (lane == 0) {
+        r.i[w] = a;
+        r.i2[w] = b;
+    }
+    __syncthreads();
+    int x = (lane < CDF_NW) ? r.i[lane] : 0, y = (lane < CDF_NW) ? r.i2[lane] : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        x += __shfl_xor_sync(0xffffffffu, x, off);
+        y += __shfl_xor_sync(0xffffffffu, y, off);
+    }
+    __syncthreads();
+    a = x;
+    b = y;
+}
+
 // (value desc, index asc) total order: the largest value, smallest index on ties.
 __device__ __forceinline__ void am_merge(float& v, int& i, float ov, int oi) {
     if (ov > v || (ov == v && oi < i)) {
@@ -394,9 +418,10 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
             }
         }
     }
-    const int deficit = T - block_sum_i(cs, red);
     if (MODE == MODE_LOHI) {
-        const int below_all = block_sum_i(below, red);
+        int tot = cs, below_all = below;
+        block_sum_i2(tot, below_all, red);
+        const int deficit = T - tot;
         if (tid == 0) {
             const uint32_t lo = (uint32_t)(below_all + (amax < sym ? deficit : 0));
             const uint32_t hi = lo + (uint32_t)(rs.csym + (amax == sym ? deficit : 0));
@@ -404,6 +429,7 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         }
         return;
     }
+    const int deficit = T - block_sum_i(cs, red);
 
     // ---- per-warp totals (deficit on the argmax's warp), exclusive scan ----
     int ws = cs;
