@@ -397,7 +397,23 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         float e[8];
         int c[8];
         int step;
-        if (i0 + 8 <= we && aligned_row) {
+        const bool full = i0 + 8 <= we && aligned_row;
+        if (full && small && (MODE != MODE_LOHI || i0 + 8 <= sym || i0 > sym)) {
+            // common case: only the chunk's total is needed; the floors are
+            // exact integers below 2^23 (their row sum is at most T - V), so
+            // they add up exactly in float, on the FMA pipe
+            src.load8_full(i0, e);
+            const float g = gs[i0 / SUBTILE];
+            float f = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                f = __fadd_rn(f, __fsub_rn(__fadd_rd(__fmul_rn(e[k], g), 8388608.0f), 8388608.0f));
+            step = __float2int_rn(f) + 8;
+            cs += step;
+            if (MODE == MODE_LOHI && i0 + 8 <= sym) below += step;
+            continue;
+        }
+        if (full) {
             src.load8_full(i0, e);
             step = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
                          : counts8_full<false>(e, gs[i0 / SUBTILE], c);
