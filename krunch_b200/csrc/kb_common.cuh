@@ -58,8 +58,8 @@ __host__ __device__ inline float kb_bits_to_float(uint32_t u) {
 #endif
 }
 
-__device__ __forceinline__ float kb_expf(float x) {
-    if (!(x >= -86.0f)) return 0.0f;
+// kb_expf without the range check, for -86 <= x <= 88.
+__device__ __forceinline__ float kb_expf_core(float x) {
     const float LOG2E = kb_bits_to_float(0x3fb8aa3bu);  // 1/ln2 rounded to fp32
     const float y = __fmul_rn(x, LOG2E);
     // n = rint(y) (half to even) without the conversion pipe: adding
@@ -74,7 +74,14 @@ __device__ __forceinline__ float kb_expf(float x) {
     p = __fmaf_rn(p, f, kb_bits_to_float(0x3e75fdf0u));  // ln2^2/2!
     p = __fmaf_rn(p, f, kb_bits_to_float(0x3f317218u));  // ln2
     p = __fmaf_rn(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
+    // bits(t) = 0x4B400000 + n; shifted left by 23 the constant part leaves
+    // 32 bits, so this adds n to p's exponent field
+    return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+__device__ __forceinline__ float kb_expf(float x) {
+    if (!(x >= -86.0f)) return 0.0f;
+    return kb_expf_core(x);
 }
 
 __device__ __forceinline__ float h2f(uint16_t h) {
