@@ -14,9 +14,9 @@ KRUNCH_PURE_WKV=1) on seeded inputs and stores what it produced:
   (krunch_b200.synth.random_weights) — full rows for the tiny model, the first
   256 logits and row summaries for RWKV-4-169M.
 
-Needs the reference tree (default /root/reference, or $KRUNCH_REFERENCE) and
+Needs the reference tree (the directory in $KRUNCH_REFERENCE) and
 torch; it is run by hand, not by the test suite:
-    python tests/golden/make_golden.py
+    KRUNCH_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -35,7 +35,7 @@ sys.path.insert(0, str(REPO))
 
 from krunch_b200.synth import random_weights  # noqa: E402
 
-REF = Path(os.environ.get("KRUNCH_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("KRUNCH_REFERENCE", "reference"))
 
 # (N, V, seed) of tests/test_ac_reference.py:63-69 and test_ac_kernel_gpu.py:57-63
 CODER_SHAPES = [(1, 4, 10), (16, 64, 11), (256, 256, 12), (1024, 1024, 13), (4096, 50277, 14),
