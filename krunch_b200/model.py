@@ -190,9 +190,11 @@ class RWKVModel:
     # ------------------------------------------------------ fused decode step
     @property
     def has_fused_step(self) -> bool:
-        """The w8a8 model decodes through kb_step_forward (one persistent
-        launch for the layer stack)."""
-        return self.spec.wdtype == "i8"
+        """The w8a8 model (up to C = 768) decodes through kb_step_forward (one
+        persistent launch for the layer stack)."""
+        # measured: at C = 2048 (1.5B, B = 512) the per-op chain is faster
+        # (4.96 vs 7.09 ms/step); at C = 768 the fused step is (0.60 vs 1.09)
+        return self.spec.wdtype == "i8" and self.spec.n_embd <= 768
 
     def new_step_workspace(self, B: int) -> torch.Tensor:
         n = int(N.load().kb_step_workspace_bytes(self.handle, B))
