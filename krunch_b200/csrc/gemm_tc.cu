@@ -526,11 +526,10 @@ template <int EPI, int BN, int KIND>
 int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs& args,
                  cudaStream_t st) {
     using Cfg = TcCfg<BN, KIND>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM);
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t attr_err = once_per_device(done, [] {
+        return cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM);
     });
     if (attr_err != cudaSuccess) {
         set_cuda_error(attr_err);

@@ -3,6 +3,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+
+#include <atomic>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -25,6 +27,20 @@ inline int launch_status() {
 }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Runs f (a cudaError_t-returning setter, e.g. a kernel's shared-memory
+// attribute) once per device of the process; idempotent if two host threads
+// race on the first call.
+template <class F>
+inline cudaError_t once_per_device(std::atomic<unsigned long long>& done, F&& f) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) dev = 0;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    const cudaError_t e = f();
+    if (e == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

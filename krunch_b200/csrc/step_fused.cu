@@ -944,15 +944,14 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
     p->h.spin_ns = g_step_fault.spin_ns ? g_step_fault.spin_ns : SF_SPIN_NS;
     p->h.withhold_arrival = g_step_fault.withhold;
 
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t attr_err = once_per_device(done, [] {
         const int sm = (int)SF_SMEM;
         cudaError_t e = cudaSuccess;
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_step_fused<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_step_fused<24>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(k_step_fused<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-        attr_err = e;
+        return e;
     });
     if (attr_err != cudaSuccess) {
         set_cuda_error(attr_err);
