@@ -72,7 +72,7 @@ def test_decode_step_batched_roundtrip(torch, B, N, V, seed):
     cat = bytearray(pos)
     for o, bs in zip(offs, streams):
         cat[o:o + len(bs)] = bs
-    inb = torch.frombuffer(bytes(cat), dtype=torch.uint8).clone().cuda()
+    inb = torch.frombuffer(bytearray(cat), dtype=torch.uint8).clone().cuda()
     offs_t = torch.tensor(offs, dtype=torch.int32, device="cuda")
     st = torch.zeros(B * 4, dtype=torch.uint32, device="cuda")
     kc.decode_init_batched(inb, offs_t, st)
