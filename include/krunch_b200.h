@@ -210,10 +210,12 @@ int kb_quantize_weight(const uint16_t* w, int N, int K, int8_t* q, uint16_t* sca
  * scale[r] = amax / 127 (fp32; 0 for an all-zero row). */
 int kb_quantize_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, void* stream);
 
-/* kb_gemm with the output tile width fixed: tile_n in {32, 64, 128, 256}, or
- * 0 for the library's choice (the widest width whose tiles fill the SMs).
- * Every width gives bit-identical results: an output element's K walk does
- * not depend on the tile shape. */
+/* kb_gemm with the output tile fixed: tile_n in {32, 64, 128, 256} for one
+ * CTA per 128-row x tile_n tile, KB_TILE_PAIR for a cluster of two CTAs per
+ * 256-row x 256-column tile (cta_group::2 MMAs; the library's choice for
+ * large M), or 0 for the library's choice.  Every tiling gives bit-identical
+ * results: an output element's K walk does not depend on the tile shape. */
+#define KB_TILE_PAIR 512
 int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* W, int64_t ldw,
                   int M, int N, int K, int epilogue, void* out, int64_t ldo,
                   const uint16_t* resid, const uint16_t* gate, int tile_n, void* stream);

@@ -19,6 +19,7 @@ KB_NOALLOC_SCRATCH_BYTES = 8 << 20
 KB_CDF_COUNTS, KB_CDF_CDF, KB_CDF_LOHI = 0, 1, 2
 KB_EPI_F32, KB_EPI_F16, KB_EPI_SIGMOID, KB_EPI_RELU_SQ, KB_EPI_RESID, KB_EPI_GATE_RESID = range(6)
 KB_F16, KB_BF16, KB_I8 = 0, 1, 2
+KB_TILE_PAIR = 512  # kb_gemm_tiled / kb_gemm_i8: CTA-pair 256 x 256 tiles
 KB_WKV_STEP_REF, KB_WKV_PRODUCTION = 0, 1
 
 vp = C.c_void_p

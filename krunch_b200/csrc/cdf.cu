@@ -399,16 +399,16 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         int step;
         const bool full = i0 + 8 <= we && aligned_row;
         if (full && small && (MODE != MODE_LOHI || i0 + 8 <= sym || i0 > sym)) {
-            // common case: only the chunk's total is needed; the floors are
-            // exact integers below 2^23 (their row sum is at most T - V), so
-            // they add up exactly in float, on the FMA pipe
+            // common case: only the chunk's total is needed.  floor(q) for
+            // 0 <= q < 2^23 is the bit pattern of q + 2^23 (rounded down)
+            // minus that of 2^23; the patterns add up in wrapping integer
+            // arithmetic and the 8 offsets come off once
             src.load8_full(i0, e);
             const float g = gs[i0 / SUBTILE];
-            float f = 0.0f;
+            uint32_t f = 8u - 8u * 0x4B000000u;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                f = __fadd_rn(f, __fsub_rn(__fadd_rd(__fmul_rn(e[k], g), 8388608.0f), 8388608.0f));
-            step = __float2int_rn(f) + 8;
+            for (int k = 0; k < 8; ++k) f += __float_as_uint(__fadd_rd(__fmul_rn(e[k], g), 8388608.0f));
+            step = (int)f;
             cs += step;
             if (MODE == MODE_LOHI && i0 + 8 <= sym) below += step;
             continue;

@@ -13,7 +13,8 @@ extern "C" int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* 
     using namespace kb;
     if (!A || !W || !out || M < 0 || N <= 0 || K <= 0) return KB_ERR_ARG;
     if (epilogue < KB_EPI_F32 || epilogue > KB_EPI_GATE_RESID) return KB_ERR_ARG;
-    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256)
+    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256 &&
+        tile_n != KB_TILE_PAIR)
         return KB_ERR_ARG;
     if (dtype != KB_F16 && dtype != KB_BF16) return KB_ERR_UNSUPPORTED;
     if (N % 32 || K % 64) return KB_ERR_SHAPE;
@@ -44,7 +45,8 @@ extern "C" int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, co
                           int tile_n, void* stream) {
     using namespace kb;
     if (!A || !W || !out || !a_scale || !w_scale || M < 0 || N <= 0 || K <= 0) return KB_ERR_ARG;
-    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256)
+    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256 &&
+        tile_n != KB_TILE_PAIR)
         return KB_ERR_ARG;
     if (epilogue < KB_EPI_F32 || epilogue > KB_EPI_GATE_RESID) return KB_ERR_ARG;
     if (N % 32 || K % 128) return KB_ERR_SHAPE;

@@ -31,7 +31,24 @@ namespace kb {
 
 constexpr int TC_BM = 128, TC_BK = 64, TC_NT = 576;
 constexpr int TC_EPI_WARPS = 16;
-constexpr uint32_t TC_STAGE_OUT = 2048;  // output staging per epilogue warp
+#ifndef TC_OUT_BUFS
+#define TC_OUT_BUFS 1
+#endif
+#ifndef TC_PAIR_AUTO
+#define TC_PAIR_AUTO 1
+#endif
+#ifndef TC_MAX_BN
+#define TC_MAX_BN 256
+#endif
+#ifndef TC_STAGE_BUDGET
+#define TC_STAGE_BUDGET 196608
+#endif
+// Output staging per epilogue warp: a ring of TC_OUT_BUFS 2 KB tiles, so a
+// warp stages the next chunk while the TMA store of the previous one still
+// reads shared memory.
+constexpr int TC_OUT_RING = TC_OUT_BUFS;
+constexpr uint32_t TC_OUT_TILE = 2048;
+constexpr uint32_t TC_STAGE_OUT = TC_OUT_TILE * TC_OUT_RING;
 constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 
 // Tile width BN in {256, 128, 64, 32}: 256 for large M; narrower tiles give
@@ -41,21 +58,27 @@ constexpr uint32_t TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
 // GEMM inputs; the kernel's tensor maps move 2-byte elements either way)
 enum { TC_F16 = 0, TC_I8 = 1, TC_BF16 = 2 };
 
-template <int BN, int KIND>
+// PAIR: a cluster of two CTAs computes a 256-row x BN tile with cta_group::2
+// MMAs; each CTA stages its 128 rows of A and BN / 2 rows of B.
+template <int BN, int KIND, bool PAIR = false>
 struct TcCfg {
     static_assert(BN == 256 || BN == 128 || BN == 64 || BN == 32, "tile width");
+    static_assert(!PAIR || BN == 256, "CTA pairs use 256-column tiles");
     // a K block is one 128-byte swizzle row: 64 fp16 or 128 int8 elements
     static constexpr int KEL = KIND == TC_I8 ? 128 : 64;
-    static constexpr uint32_t B_BYTES = BN * 128;
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B staged by this CTA
+    static constexpr int BM = PAIR ? 2 * TC_BM : TC_BM;  // rows of an output tile
+    static constexpr uint32_t B_BYTES = B_ROWS * 128;
     static constexpr uint32_t STAGE_BYTES = TC_A_BYTES + B_BYTES;
-    static constexpr int STAGES = (196608 / STAGE_BYTES) < 8 ? (196608 / STAGE_BYTES) : 8;
+    static constexpr int STAGES =
+        (TC_STAGE_BUDGET / STAGE_BYTES) < 8 ? (TC_STAGE_BUDGET / STAGE_BYTES) : 8;
     static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators
     static constexpr size_t SMEM = (size_t)STAGES * STAGE_BYTES +
                                    TC_EPI_WARPS * TC_STAGE_OUT /*output staging*/ +
                                    1024 /*align*/ + 256 /*bars*/;
     static_assert(SMEM <= 232448, "shared memory per block");
     static constexpr uint32_t IDESC =
-        KIND == TC_I8 ? tc::idesc_i8(TC_BM, BN) : tc::idesc_f16(TC_BM, BN, KIND == TC_BF16);
+        KIND == TC_I8 ? tc::idesc_i8(BM, BN) : tc::idesc_f16(BM, BN, KIND == TC_BF16);
 };
 
 // Launch parameters of one GEMM (a __grid_constant__ kernel argument).
@@ -93,16 +116,43 @@ __device__ __forceinline__ bool tc_aborted(TcBars* b) {
 
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
+#ifdef TC_DIAG
+// cycles spent in each wait, summed over the threads that wait:
+// 0 producer/empty, 1 mma/tempty, 2 mma/full, 3 epilogue/tfull,
+// 4 epilogue/staging, 5 epilogue busy (tfull done -> tempty arrive), 6 mma loop
+__device__ unsigned long long g_tc_diag[8];
+}  // namespace kb
+// diagnostic build only: copy (and optionally clear) the wait-cycle sums
+extern "C" int kb_tc_diag(unsigned long long* host_out, int reset) {
+    cudaDeviceSynchronize();
+    if (cudaMemcpyFromSymbol(host_out, kb::g_tc_diag, sizeof(kb::g_tc_diag)) != cudaSuccess)
+        return -1;
+    if (reset) {
+        static const unsigned long long z[8] = {};
+        cudaMemcpyToSymbol(kb::g_tc_diag, z, sizeof(z));
+    }
+    return 0;
+}
+namespace kb {
+#define DIAG_T0(v) const long long v = clock64()
+#define DIAG_ADD(acc, v) acc += (unsigned long long)(clock64() - (v))
+#define DIAG_FLUSH(i, acc) atomicAdd(&g_tc_diag[i], acc)
+#else
+#define DIAG_T0(v)
+#define DIAG_ADD(acc, v)
+#define DIAG_FLUSH(i, acc)
+#endif
+
 // Tile order: groups of TC_GROUP_M row blocks; inside a group the row block
 // changes fastest, so the CTAs running at the same time share a few weight
 // tiles (read from L2) and a few activation row blocks.
 constexpr int TC_GROUP_M = 16;
-template <int BN>
+template <int BN, int BM = TC_BM>
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& m0, int& n0) {
     const int per_group = TC_GROUP_M * num_n;
     const int g = t / per_group, r = t - g * per_group;
     const int gm = min(TC_GROUP_M, num_m - g * TC_GROUP_M);
-    m0 = (g * TC_GROUP_M + r % gm) * TC_BM;
+    m0 = (g * TC_GROUP_M + r % gm) * BM;
     n0 = (r / gm) * BN;
 }
 
@@ -117,13 +167,25 @@ __device__ __forceinline__ void stage_row64(unsigned char* st, int r, const uint
             make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
-// Warp-wide: wait until the staging tile is free, stage this lane's row,
+// Warp-wide: the next tile of this warp's staging ring, once the store
+// issued from it TC_OUT_RING stores ago has finished reading it.
+__device__ __forceinline__ unsigned char* out_tile(unsigned char* ring, uint32_t& n, int lane) {
+    if (lane == 0) {
+        DIAG_T0(t0);
+        tc::bulk_wait_read_max<TC_OUT_RING - 1>();
+#ifdef TC_DIAG
+        atomicAdd(&g_tc_diag[4], (unsigned long long)(clock64() - t0));
+#endif
+    }
+    __syncwarp();
+    return ring + (n++ % TC_OUT_RING) * TC_OUT_TILE;
+}
+
+// Warp-wide: stage this lane's row in a free staging tile (out_tile()),
 // store the tile at (c0, r0).
 __device__ __forceinline__ void stage_and_store(unsigned char* st, int lane,
                                                 const uint32_t (&w)[16], const CUtensorMap* map,
                                                 int c0, int r0) {
-    if (lane == 0) tc::bulk_wait_read();
-    __syncwarp();
     stage_row64(st, lane, w);
     tc::fence_proxy_async_smem();
     __syncwarp();
@@ -134,12 +196,10 @@ __device__ __forceinline__ void stage_and_store(unsigned char* st, int lane,
 }
 
 // Warp-wide coalesced read of a 32-row x 32-column fp16 tile (rows from r0,
-// rows >= M read as zero) through the staging buffer; lane i gets row r0 + i.
+// rows >= M read as zero) through a free staging tile; lane i gets row r0 + i.
 __device__ __forceinline__ void load_tile_rows(const uint16_t* src, int64_t ld, int64_t r0, int c0,
                                                int M, unsigned char* st, int lane,
                                                uint4 (&out)[4]) {
-    if (lane == 0) tc::bulk_wait_read();
-    __syncwarp();
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const int idx = k * 32 + lane, r = idx >> 2, j = idx & 3;
@@ -214,11 +274,11 @@ __device__ __forceinline__ void dequant32(uint32_t (&v)[32], float sa, const uin
     }
 }
 
-template <int EPI, int BN, int KIND>
+template <int EPI, int BN, int KIND, bool PAIR>
 __global__ void __launch_bounds__(TC_NT, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
               const __grid_constant__ CUtensorMap mapO, const __grid_constant__ TcArgs args) {
-    using Cfg = TcCfg<BN, KIND>;
+    using Cfg = TcCfg<BN, KIND, PAIR>;
     const int M = args.M, N = args.N, K = args.K;
     const int64_t ldo = args.ldo;
     const int V = args.V, stats_stride = args.stats_stride;
@@ -233,9 +293,13 @@ __global__ void __launch_bounds__(TC_NT, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_n = (N + BN - 1) / BN;
-    const int num_m = (M + TC_BM - 1) / TC_BM;
+    const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
     const int tiles = num_m * num_n;
     const int KB = K / Cfg::KEL;
+    // a pair walks the tiles as one unit; rank 1 holds rows 128..255 of each
+    const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
+    const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < TC_STAGES; ++s) {
@@ -244,7 +308,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
         }
         for (int a = 0; a < 2; ++a) {
             tc::mbar_init(&bars->tfull[a], 1);
-            tc::mbar_init(&bars->tempty[a], TC_EPI_WARPS);
+            tc::mbar_init(&bars->tempty[a], PAIR ? 2 * TC_EPI_WARPS : TC_EPI_WARPS);
         }
         bars->abort = 0;
         tc::fence_barrier_init();
@@ -254,9 +318,13 @@ __global__ void __launch_bounds__(TC_NT, 1)
         tc::prefetch_tmap(&mapB);
         tc::prefetch_tmap(&mapO);
     }
-    if (warp == 1) tc::tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
+    if (warp == 1) {
+        if (PAIR) tc::tmem_alloc_pair(&bars->tmem_base, Cfg::TMEM_COLS);
+        else tc::tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
+    }
     tc::fence_before_sync();
     __syncthreads();
+    if (PAIR) tc::cluster_sync();  // the peer's barriers are initialised
     tc::fence_after_sync();
     const uint32_t tmem = bars->tmem_base;
 
@@ -266,18 +334,34 @@ __global__ void __launch_bounds__(TC_NT, 1)
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued = 0, issued_parity = 0;  // per-stage bit masks
-            for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x) {
+#ifdef TC_DIAG
+            unsigned long long d_empty = 0;
+#endif
+            for (int t = unit0; t < tiles && !tc_aborted(bars); t += units) {
                 int m0, n0;
-                tile_coords<BN>(t, num_m, num_n, m0, n0);
+                tile_coords<BN, Cfg::BM>(t, num_m, num_n, m0, n0);
                 for (int kb = 0; kb < KB; ++kb) {
-                    if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1u)) {
+                    DIAG_T0(tw);
+                    const bool okw = tc::mbar_wait(&bars->empty[stage], phase ^ 1u);
+                    DIAG_ADD(d_empty, tw);
+                    if (!okw) {
                         tc_fail(bars, 1);
                         break;
                     }
                     unsigned char* sa = smem + stage * TC_STAGE_BYTES;
-                    tc::mbar_expect_tx(&bars->full[stage], TC_STAGE_BYTES);
-                    tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * Cfg::KEL, m0);
-                    tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * Cfg::KEL, n0);
+                    if (PAIR) {
+                        // both CTAs' bytes complete on the leader's barrier
+                        const uint32_t fb = tc::mapa_shared(tc::smem_addr(&bars->full[stage]), 0);
+                        if (rank == 0) tc::mbar_expect_tx(&bars->full[stage], 2 * TC_STAGE_BYTES);
+                        tc::tma_load_2d_pair(sa, &mapA, fb, kb * Cfg::KEL, m0 + (int)rank * TC_BM);
+                        tc::tma_load_2d_pair(sa + TC_A_BYTES, &mapB, fb, kb * Cfg::KEL,
+                                             n0 + (int)rank * Cfg::B_ROWS);
+                    } else {
+                        tc::mbar_expect_tx(&bars->full[stage], TC_STAGE_BYTES);
+                        tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * Cfg::KEL, m0);
+                        tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * Cfg::KEL,
+                                        n0);
+                    }
                     issued |= 1u << stage;
                     issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == TC_STAGES) {
@@ -286,21 +370,34 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     }
                 }
             }
+            DIAG_FLUSH(0, d_empty);
             // Drain: every load this thread issued has landed before the CTA
             // exits (immediate on the normal path; bounded after an abort).
+            // A pair's rank 1 sees its loads through the leader's barrier, so
+            // it waits for the MMAs that consumed them.
             for (int s = 0; s < TC_STAGES; ++s)
-                if (issued & (1u << s)) tc::mbar_wait(&bars->full[s], (issued_parity >> s) & 1u);
+                if (issued & (1u << s)) {
+                    if (PAIR && rank != 0) tc::mbar_wait(&bars->empty[s], (issued_parity >> s) & 1u);
+                    else tc::mbar_wait(&bars->full[s], (issued_parity >> s) & 1u);
+                }
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (a pair's leader) ----------------
+        if (lane == 0 && rank == 0) {
             int stage = 0;
             uint32_t phase = 0;
             int i = 0;
-            for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
+#ifdef TC_DIAG
+            unsigned long long d_tempty = 0, d_full = 0, d_loop = 0;
+            DIAG_T0(tl);
+#endif
+            for (int t = unit0; t < tiles && !tc_aborted(bars); t += units, ++i) {
                 const int a = i & 1;
                 const uint32_t use = (uint32_t)(i >> 1);
-                if (!tc::mbar_wait(&bars->tempty[a], (use & 1u) ^ 1u)) {
+                DIAG_T0(tw);
+                const bool okt = tc::mbar_wait(&bars->tempty[a], (use & 1u) ^ 1u);
+                DIAG_ADD(d_tempty, tw);
+                if (!okt) {
                     tc_fail(bars, 2);
                     break;
                 }
@@ -308,7 +405,10 @@ __global__ void __launch_bounds__(TC_NT, 1)
                 const uint32_t d = tmem + (uint32_t)(a * BN);
                 bool ok = true;
                 for (int kb = 0; kb < KB; ++kb) {
-                    if (!tc::mbar_wait(&bars->full[stage], phase)) {
+                    DIAG_T0(tf);
+                    const bool okf = tc::mbar_wait(&bars->full[stage], phase);
+                    DIAG_ADD(d_full, tf);
+                    if (!okf) {
                         tc_fail(bars, 3);
                         ok = false;
                         break;
@@ -318,35 +418,64 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     const uint32_t sb = sa + TC_A_BYTES;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {  // 32 bytes of K per MMA
-                        if (KIND == TC_I8)
-                            tc::mma_i8(d, tc::sdesc_k128(sa + 32u * j),
-                                       tc::sdesc_k128(sb + 32u * j), Cfg::IDESC, (kb | j) != 0);
-                        else
-                            tc::mma_f16(d, tc::sdesc_k128(sa + 32u * j),
-                                        tc::sdesc_k128(sb + 32u * j), Cfg::IDESC, (kb | j) != 0);
+                        const uint64_t ad = tc::sdesc_k128(sa + 32u * j);
+                        const uint64_t bd = tc::sdesc_k128(sb + 32u * j);
+                        const uint32_t acc = (kb | j) != 0;
+                        if (PAIR) {
+                            if (KIND == TC_I8) tc::mma_i8_pair(d, ad, bd, Cfg::IDESC, acc);
+                            else tc::mma_f16_pair(d, ad, bd, Cfg::IDESC, acc);
+                        } else {
+                            if (KIND == TC_I8) tc::mma_i8(d, ad, bd, Cfg::IDESC, acc);
+                            else tc::mma_f16(d, ad, bd, Cfg::IDESC, acc);
+                        }
                     }
-                    tc::mma_commit(&bars->empty[stage]);
+                    if (PAIR) {  // the stage is free in both CTAs
+                        const uint32_t eb = tc::smem_addr(&bars->empty[stage]);
+                        tc::mma_commit_pair(tc::mapa_shared(eb, 0));
+                        tc::mma_commit_pair(tc::mapa_shared(eb, 1));
+                    } else {
+                        tc::mma_commit(&bars->empty[stage]);
+                    }
                     if (++stage == TC_STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                tc::mma_commit(&bars->tfull[a]);
+                if (PAIR) {
+                    const uint32_t fb = tc::smem_addr(&bars->tfull[a]);
+                    tc::mma_commit_pair(tc::mapa_shared(fb, 0));
+                    tc::mma_commit_pair(tc::mapa_shared(fb, 1));
+                } else {
+                    tc::mma_commit(&bars->tfull[a]);
+                }
             }
+            DIAG_ADD(d_loop, tl);
+            DIAG_FLUSH(1, d_tempty);
+            DIAG_FLUSH(2, d_full);
+            DIAG_FLUSH(6, d_loop);
         }
     } else {
         // ---------------- epilogue (warps 2..17) ----------------
         const int q = warp & 3;          // TMEM lane quadrant this warp may access
         const int g = (warp - 2) >> 2;   // quarter of the tile's columns
-        unsigned char* st = stage_out + (warp - 2) * TC_STAGE_OUT;
+        unsigned char* const ring = stage_out + (warp - 2) * TC_STAGE_OUT;
+        uint32_t nst = 0;  // stores issued from the ring
         int i = 0;
-        for (int t = blockIdx.x; t < tiles && !tc_aborted(bars); t += gridDim.x, ++i) {
+#ifdef TC_DIAG
+        unsigned long long d_tfull = 0, d_busy = 0;
+#endif
+        for (int t = unit0; t < tiles && !tc_aborted(bars); t += units, ++i) {
             const int a = i & 1;
             const uint32_t use = (uint32_t)(i >> 1);
-            int m0, n0;
-            tile_coords<BN>(t, num_m, num_n, m0, n0);
-            if (!tc::mbar_wait(&bars->tfull[a], use & 1u)) {
+            int mt, n0;
+            tile_coords<BN, Cfg::BM>(t, num_m, num_n, mt, n0);
+            const int m0 = mt + (int)rank * TC_BM;  // this CTA's 128 rows
+            DIAG_T0(tw);
+            const bool okt = tc::mbar_wait(&bars->tfull[a], use & 1u);
+            DIAG_ADD(d_tfull, tw);
+            DIAG_T0(tb);
+            if (!okt) {
                 tc_fail(bars, 4);
                 break;
             }
@@ -408,7 +537,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
                             packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
                         }
                     }
-                    stage_and_store(st, lane, packed, &mapO, col0, m0 + q * 32);
+                    stage_and_store(out_tile(ring, nst, lane), lane, packed, &mapO, col0,
+                                    m0 + q * 32);
                     if (row < M) {
                         const int u = col0 / SUBTILE;
                         if (u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
@@ -429,11 +559,13 @@ __global__ void __launch_bounds__(TC_NT, 1)
                             uint32_t w[16];
 #pragma unroll
                             for (int j = 0; j < 16; ++j) w[j] = v[16 * h + j];
-                            stage_and_store(st, lane, w, &mapO, col0 + 16 * h, m0 + q * 32);
+                            stage_and_store(out_tile(ring, nst, lane), lane, w, &mapO,
+                                            col0 + 16 * h, m0 + q * 32);
                         }
                     } else {
                         uint32_t w[16];
                         uint4 rv[4], gv[4];
+                        unsigned char* const st = out_tile(ring, nst, lane);
                         if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID)
                             load_tile_rows(args.resid, ldo, m0 + q * 32, col0, M, st, lane, rv);
                         if (EPI == KB_EPI_GATE_RESID)
@@ -446,16 +578,26 @@ __global__ void __launch_bounds__(TC_NT, 1)
             }
             tc::fence_before_sync();
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&bars->tempty[a]);
+            if (lane == 0) {
+                if (PAIR) tc::mbar_arrive_cluster(tc::mapa_shared(tc::smem_addr(&bars->tempty[a]), 0));
+                else tc::mbar_arrive(&bars->tempty[a]);
+            }
+            DIAG_ADD(d_busy, tb);
+        }
+        if (lane == 0) {
+            DIAG_FLUSH(3, d_tfull);
+            DIAG_FLUSH(5, d_busy);
         }
         if (lane == 0) tc::bulk_wait_all();  // staged stores done before exit
     }
 
     tc::fence_before_sync();
     __syncthreads();
+    if (PAIR) tc::cluster_sync();  // no CTA leaves while its peer may still signal it
     if (warp == 1) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
+        if (PAIR) tc::tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+        else tc::tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
 }
 
@@ -522,13 +664,41 @@ int sm_count() {
     return cache[dev];
 }
 
-template <int EPI, int BN, int KIND>
+// Clusters of two CTAs of a pair kernel that fit on the device at once (the
+// pair kernel's grid), cached per device.
+template <class Kern>
+int pair_clusters(Kern kern, size_t smem, std::atomic<int>* cache) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    int n = cache[dev].load();
+    if (n) return n;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(TC_NT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = -1;  // pairs unavailable: callers fall back to single CTAs
+    }
+    cache[dev].store(n);
+    return n;
+}
+
+template <int EPI, int BN, int KIND, bool PAIR>
 int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs& args,
                  cudaStream_t st) {
-    using Cfg = TcCfg<BN, KIND>;
+    using Cfg = TcCfg<BN, KIND, PAIR>;
     static std::atomic<unsigned long long> done{0};
     const cudaError_t attr_err = once_per_device(done, [] {
-        return cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND>,
+        return cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND, PAIR>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Cfg::SMEM);
     });
     if (attr_err != cudaSuccess) {
@@ -536,22 +706,58 @@ int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs
         return KB_ERR_CUDA;
     }
     CUtensorMap mb, mo;
-    if (!make_map(&mb, W, args.N, args.K, ldw, BN, KIND == TC_I8 ? 1 : 2) ||
+    if (!make_map(&mb, W, args.N, args.K, ldw, Cfg::B_ROWS, KIND == TC_I8 ? 1 : 2) ||
         !make_out_map(&mo, args.out, args.M, args.N, args.ldo, EPI == KB_EPI_F32 ? 4 : 2))
         return KB_ERR_UNSUPPORTED;
-    const int tiles = ((args.M + TC_BM - 1) / TC_BM) * ((args.N + BN - 1) / BN);
-    const int grid = tiles < sm_count() ? tiles : sm_count();
-    k_gemm_tc<EPI, BN, KIND><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, mo, args);
+    const int tiles = ((args.M + Cfg::BM - 1) / Cfg::BM) * ((args.N + BN - 1) / BN);
+    if constexpr (!PAIR) {
+        const int grid = tiles < sm_count() ? tiles : sm_count();
+        k_gemm_tc<EPI, BN, KIND, false><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, mo, args);
+        return launch_status();
+    } else {
+    static std::atomic<int> clusters[64];
+    const int nc = pair_clusters(k_gemm_tc<EPI, BN, KIND, true>, Cfg::SMEM, clusters);
+    if (nc <= 0) return KB_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (tiles < nc ? tiles : nc));
+    cfg.blockDim = dim3(TC_NT);
+    cfg.dynamicSmemBytes = Cfg::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, BN, KIND, true>, ma, mb, mo, args);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return KB_ERR_CUDA;
+    }
     return launch_status();
+    }
 }
 
 // Tile width for a launch: the widest whose tile count fills the SMs, else
 // the narrowest.  Every width gives the same bits (one K walk per element).
 int pick_bn(int M, int N) {
     const int mt = (M + TC_BM - 1) / TC_BM, sms = sm_count();
-    for (int bn = 256; bn > 32; bn >>= 1)
+    for (int bn = TC_MAX_BN; bn > 32; bn >>= 1)
         if (mt * ((N + bn - 1) / bn) >= sms) return bn;
     return 32;
+}
+
+// Library choice: CTA pairs (256 x 256 tiles) once their tiles fill every
+// pair of SMs at least twice over, else pick_bn's single-CTA width.  The head
+// (softmax-numerator epilogue, bound by its exponentials) measured faster on
+// single CTAs and keeps them.
+int pick_tile(int M, int N, bool logits) {
+    const int bn = pick_bn(M, N);
+    if (TC_PAIR_AUTO && bn == 256 && ((M + 255) / 256) * ((N + 255) / 256) >= sm_count() &&
+        !logits)
+        return KB_TILE_PAIR;
+    return bn;
 }
 
 template <int EPI, int KIND>
@@ -560,12 +766,17 @@ int launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, const TcAr
     CUtensorMap ma;
     if (!make_map(&ma, A, args.M, args.K, lda, TC_BM, KIND == TC_I8 ? 1 : 2))
         return KB_ERR_UNSUPPORTED;
-    if (bn == 0) bn = pick_bn(args.M, args.N);
+    if (bn == 0) bn = pick_tile(args.M, args.N, EPI == KB_EPI_LOGITS_STATS);
     switch (bn) {
-        case 256: return launch_tc_bn<EPI, 256, KIND>(ma, W, ldw, args, st);
-        case 128: return launch_tc_bn<EPI, 128, KIND>(ma, W, ldw, args, st);
-        case 64: return launch_tc_bn<EPI, 64, KIND>(ma, W, ldw, args, st);
-        case 32: return launch_tc_bn<EPI, 32, KIND>(ma, W, ldw, args, st);
+        case KB_TILE_PAIR: {
+            const int r = launch_tc_bn<EPI, 256, KIND, true>(ma, W, ldw, args, st);
+            if (r != KB_ERR_UNSUPPORTED) return r;
+            return launch_tc_bn<EPI, 256, KIND, false>(ma, W, ldw, args, st);
+        }
+        case 256: return launch_tc_bn<EPI, 256, KIND, false>(ma, W, ldw, args, st);
+        case 128: return launch_tc_bn<EPI, 128, KIND, false>(ma, W, ldw, args, st);
+        case 64: return launch_tc_bn<EPI, 64, KIND, false>(ma, W, ldw, args, st);
+        case 32: return launch_tc_bn<EPI, 32, KIND, false>(ma, W, ldw, args, st);
         default: return KB_ERR_ARG;
     }
 }

@@ -102,7 +102,7 @@ def test_gemm_i8_epilogues_and_tile_invariance(torch, epi):
     want = _gemm8(torch, qa, sa, qw, sw, epi, 256, r, gt)
     tol = 0 if epi == 0 else 2e-2
     assert (want.float() - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
-    for tn in (128, 64, 32, 0):
+    for tn in (128, 64, 32, 0, N.KB_TILE_PAIR):
         assert torch.equal(_gemm8(torch, qa, sa, qw, sw, epi, tn, r, gt), want), tn
     # M invariance: a subset of rows alone gives the same bits
     sub = _gemm8(torch, qa[:33].contiguous(), sa[:33].contiguous(), qw, sw, epi, 0,
@@ -224,3 +224,17 @@ def test_fused_step_bounded_wait_reports_timeout(torch):
     m.step_forward(tok, st_b, ws, lb)
     torch.cuda.synchronize()
     assert torch.equal(la, lb) and torch.equal(st_a, st_b)
+
+
+@pytest.mark.parametrize("M", [256, 12345, 40000])
+def test_gemm_i8_cta_pair_exact(torch, M):
+    """CTA-pair int8 tiles: the exact integer result of the single-CTA kernel."""
+    from krunch_b200 import _native as N
+    qa, sa, qw, sw = _operands(torch, M, 768, 768, M)
+    want = _gemm8(torch, qa, sa, qw, sw, N.KB_EPI_F32, 256)
+    assert torch.equal(_gemm8(torch, qa, sa, qw, sw, N.KB_EPI_F32, N.KB_TILE_PAIR), want)
+    if M <= 12345:
+        acc = qa.cpu().numpy().astype(np.int64) @ qw.cpu().numpy().astype(np.int64).T
+        ref = (acc.astype(np.float32) * sa.cpu().numpy()[:, None]) * \
+            sw.cpu().numpy().astype(np.float32)[None, :]
+        assert np.array_equal(want.cpu().numpy(), ref.astype(np.float32))
