@@ -34,6 +34,9 @@ constexpr int TC_EPI_WARPS = 16;
 #ifndef TC_OUT_BUFS
 #define TC_OUT_BUFS 1
 #endif
+#ifndef TC_HEAD_PAIRCVT
+#define TC_HEAD_PAIRCVT 1  // head numerators converted two at a time
+#endif
 #ifndef TC_PAIR_AUTO
 #define TC_PAIR_AUTO 1
 #endif
@@ -513,11 +516,17 @@ __global__ void __launch_bounds__(TC_NT, 1)
                         for (int j = 0; j < 32; ++j) m = fmaxf(m, xr[j]);
 #pragma unroll
                         for (int j = 0; j < 32; j += 2) {
+#if TC_HEAD_PAIRCVT
+                            float f0, f1;
+                            packed[j / 2] = exp_rel_pair(xr[j], xr[j + 1], m, f0, f1);
+                            s = __fadd_rn(__fadd_rn(s, f0), f1);
+#else
                             const uint16_t e0 = exp_rel_f16(xr[j], m);
                             const uint16_t e1 = exp_rel_f16(xr[j + 1], m);
                             s = __fadd_rn(s, h2f(e0));
                             s = __fadd_rn(s, h2f(e1));
                             packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
+#endif
                         }
                     } else {
 #pragma unroll

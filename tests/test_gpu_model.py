@@ -110,6 +110,25 @@ def test_large_window_strips_match_small(torch):
         assert np.array_equal(one[0], big[b]), b
 
 
+@pytest.mark.parametrize("wdtype", ["f16", "bf16"])
+def test_large_window_odd_streams_with_state(torch, wdtype):
+    """Strips of 4 rows are computed two rows at a time; with an odd
+    window length a row pair straddles two streams, and the first row of
+    every stream takes its token-shift input from the carried state.  The
+    result equals the same tokens run as two smaller windows (1 row per
+    warp), bit for bit, state included."""
+    from krunch_b200.model import RWKVModel
+    m = RWKVModel(random_weights(2, 128, 512, 300, seed=10), wdtype=wdtype)
+    tok = np.random.default_rng(6).integers(0, 300, (77, 996))
+    _, st0 = _run(torch, m, tok[:, :3])
+    big, st_big = _run(torch, m, tok[:, 3:], st0.clone())
+    assert tok.shape[0] * (tok.shape[1] - 3) >= 148 * 8 * 64
+    a, st = _run(torch, m, tok[:, 3:500], st0.clone())
+    b, st = _run(torch, m, tok[:, 500:], st)
+    assert np.array_equal(np.concatenate([a, b], 1), big)
+    assert torch.equal(st, st_big)
+
+
 @pytest.mark.parametrize("wdtype", ["f16", "i8"])
 def test_wide_rows_vs_oracle_and_stepped(torch, wdtype):
     """C = 2048 (the 1.5B width) runs LayerNorm+mix in the streaming kernel:
