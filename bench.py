@@ -301,15 +301,22 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev.index) as clk:
-        N.profile_begin()
         e0.record(stream)
         for _ in range(args.steps):
             plan.run()
         e1.record(stream)
         torch.cuda.synchronize()
-        prof = N.profile_end()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    # the same K steps again with every launch bracketed by CUDA events (the
+    # per-kernel durations of the roofline); a separate pass because events
+    # between launches keep a kernel from starting during the previous one's
+    # tail (programmatic dependent launch), which the headline pass allows
+    N.profile_begin()
+    for _ in range(args.steps):
+        plan.run()
+    torch.cuda.synchronize()
+    prof = N.profile_end()
     streams = plan.fetch()
     comp_bytes = sum(len(s) for s in streams)
     tokens_all = args.B * args.T * world

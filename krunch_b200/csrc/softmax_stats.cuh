@@ -38,12 +38,8 @@ __device__ __forceinline__ MS ms_shfl_xor(MS v, int off) {
 }
 
 // e_i of a logit relative to its subtile max, as stored (fp16 bits).
-// kb_expf returns 0 below -86 (and for NaN); any value under 2^-25 rounds to
-// fp16 zero, so clamping the argument at -87 (fmaxf also maps NaN there; the
-// core is exact-form down to there) stores the same bits with one instruction
-// instead of a compare and a select.
 __device__ __forceinline__ float exp_rel_core(float x, float m) {
-    return kb_expf_core(fmaxf(__fsub_rn(x, m), -87.0f));
+    return kb_expf(__fsub_rn(x, m));
 }
 __device__ __forceinline__ uint16_t exp_rel_f16(float x, float m) {
     return f2h(exp_rel_core(x, m));
