@@ -50,7 +50,7 @@ SHAPE = SHAPES["169m"]
 # capture of the ffn-key GEMM (k_gemm_tc<3,256,0>, M = 16384 rows: 30.0 MB
 # read + 50.0 MB written) scaled by 4 to the bench's 65536-row launches
 # (traffic grows with M).
-GEMM_TRAFFIC = 4 * (29.998336e6 + 49.994240e6)
+GEMM_TRAFFIC = 4 * (29.979136e6 + 50.308352e6)
 GEMM_TRAFFIC_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of the ffn-key GEMM at "
                      "M=16384 x4 = per 65536-row launch; algorithmic 4 x (25.2 + 4.7 + 100.7) MB")
 
