@@ -295,6 +295,16 @@ int kb_forward_window(const kb_model* model, const int32_t* tokens, int B, int T
                       float* state, void* workspace, size_t workspace_bytes,
                       uint16_t* logits, float* logit_stats, void* stream);
 
+/* One layer of the model on a window: x fp16 [B*T, C] (rows b*T + t, 16-byte
+ * aligned) is read and replaced by the layer's output; layer_state is that
+ * layer's fp32 [5][B][C] slice of the state above (advanced in place);
+ * workspace as for kb_forward_window.  kb_forward_window is embed, this for
+ * every layer, then LayerNorm + head, so a chain of kb_layer_forward calls
+ * gives the same bits.  Replaces rwkv4_layer_step_cpp and
+ * rwkv4_layer_step_cpp_t1 (krunch_ac/cuda/layer_cpp.cpp:294-307,456-637). */
+int kb_layer_forward(const kb_model* model, int layer, uint16_t* x, int B, int T,
+                     float* layer_state, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Fused stepped decode forward (T = 1) of a KB_I8 model: the whole layer
  * stack in one persistent cooperative launch (one CTA per SM, grid barriers
  * between phases, tcgen05 kind::i8 GEMM tiles with int8 weights staged

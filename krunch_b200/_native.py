@@ -78,6 +78,7 @@ SIGNATURES = {
     "kb_state_init": (i32, [vp, vp, i32, vp]),
     "kb_forward_workspace_bytes": (sz, [vp, i32, i32]),
     "kb_forward_window": (i32, [vp, vp, i32, i32, vp, vp, sz, vp, vp, vp]),
+    "kb_layer_forward": (i32, [vp, i32, vp, i32, i32, vp, vp, sz, vp]),
     "kb_forward_window_noalloc": (i32, [vp, vp, i32, i32, vp, vp, vp]),
 }
 

@@ -202,25 +202,16 @@ size_t layout(const kb_model_desc& d, int B, int T, char* base, Workspace* w) {
 
 }  // namespace
 
-extern "C" size_t kb_forward_workspace_bytes(const kb_model* m, int B, int T) {
-    if (!m || B <= 0 || T <= 0) return 0;
-    return layout(m->d, B, T, nullptr, nullptr);
-}
+namespace {
 
-extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B, int T,
-                                 float* state, void* ws, size_t ws_bytes, uint16_t* logits,
-                                 float* logit_stats, void* stream) {
-    if (!m || !tokens || !state || !ws || !logits || B <= 0 || T <= 0) return KB_ERR_ARG;
-    const kb_model_desc& d = m->d;
-    if (ws_bytes < layout(d, B, T, nullptr, nullptr)) return KB_ERR_WORKSPACE;
-    if (!aligned16(ws) || !aligned16(logits) || ((uintptr_t)logit_stats & 7u)) return KB_ERR_ALIGN;
-    cudaStream_t st = as_stream(stream);
-    Workspace w;
-    layout(d, B, T, reinterpret_cast<char*>(ws), &w);
+// One RWKV-4 layer over a window of B x T rows, residual stream in w.x
+// (fp16 [B*T, C], read and updated), layer state s fp32 [5][B][C].  The
+// body of the reference's rwkv4_layer_step_cpp (layer_cpp.cpp:456-637).
+int run_layer(const kb_model_desc& d, const kb_layer_desc& L, const Workspace& w, int B, int T,
+              float* s, cudaStream_t st) {
     const int C = d.n_embd, F = d.n_ffn;
     const int R = B * T;
     const size_t BC = (size_t)B * C;
-
     const bool i8 = d.wdtype == KB_I8;
     const bool bf = d.wdtype == KB_BF16;  // GEMM operands (mix outputs, r*y, relu^2) in bf16
     const double bpe = 2.0;  // fp16 bytes per activation element
@@ -243,66 +234,91 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
         ProfScope ps(PH_LN_MIX, st, (double)R * K * 3.0);
         return launch_quant_rows(x, R, K, q, qs, st);
     };
+    float *s_att = s, *s_aa = s + BC, *s_bb = s + 2 * BC, *s_pp = s + 3 * BC,
+          *s_ffn = s + 4 * BC;
+
+    // ---- time mix -------------------------------------------------------
+    MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx},
+               {w.q_kx, w.q_vx, w.q_rx}, {w.s_kx, w.s_vx, w.s_rx}, bf ? 1 : 0};
+    {
+        ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? 2 * bpe + 3 : 4 * bpe));
+        KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
+    }
+    if (i8) {
+        KB_TRY(gemm8(w.q_kx, w.s_kx, L.att_kw, L.att_ks, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm8(w.q_vx, w.s_vx, L.att_vw, L.att_vs, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm8(w.q_rx, w.s_rx, L.att_rw, L.att_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+    } else {
+        KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+    }
+    {
+        ProfScope ps(PH_WKV, st, (double)R * C * 12.0);
+        KB_TRY(launch_wkv(d.wkv_convention, B, T, C, w.k, w.v, w.r, L.att_decay, L.att_first,
+                          s_aa, s_bb, s_pp, w.ry, st, bf));
+    }
+    if (i8) {
+        KB_TRY(quant(w.ry, C, w.q_ry, w.s_ry));
+        KB_TRY(gemm8(w.q_ry, w.s_ry, L.att_ow, L.att_os, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+    } else {
+        KB_TRY(gemm(w.ry, L.att_ow, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
+    }
+    if (cudaMemcpyAsync(s_att, w.xx_att, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return launch_status();
+
+    // ---- channel mix ----------------------------------------------------
+    MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr},
+               {w.q_kx, w.q_rx, nullptr}, {w.s_kx, w.s_rx, nullptr}, bf ? 1 : 0};
+    {
+        ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 2 : 3 * bpe));
+        KB_TRY(launch_ln_mix(2, w.x, B, T, C, L.ln2_w, L.ln2_b, mf, s_ffn, w.xx_ffn, nullptr, st));
+    }
+    if (i8) {
+        KB_TRY(gemm8(w.q_rx, w.s_rx, L.ffn_rw, L.ffn_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm8(w.q_kx, w.s_kx, L.ffn_kw, L.ffn_ks, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
+        KB_TRY(quant(w.kk, F, w.q_kk, w.s_kk));
+        KB_TRY(gemm8(w.q_kk, w.s_kk, L.ffn_vw, L.ffn_vs, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+    } else {
+        KB_TRY(gemm(w.rx, L.ffn_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.kx, L.ffn_kw, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
+        KB_TRY(gemm(w.kk, L.ffn_vw, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
+    }
+    if (cudaMemcpyAsync(s_ffn, w.xx_ffn, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return launch_status();
+    return KB_OK;
+}
+
+}  // namespace
+
+extern "C" size_t kb_forward_workspace_bytes(const kb_model* m, int B, int T) {
+    if (!m || B <= 0 || T <= 0) return 0;
+    return layout(m->d, B, T, nullptr, nullptr);
+}
+
+extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B, int T,
+                                 float* state, void* ws, size_t ws_bytes, uint16_t* logits,
+                                 float* logit_stats, void* stream) {
+    if (!m || !tokens || !state || !ws || !logits || B <= 0 || T <= 0) return KB_ERR_ARG;
+    const kb_model_desc& d = m->d;
+    if (ws_bytes < layout(d, B, T, nullptr, nullptr)) return KB_ERR_WORKSPACE;
+    if (!aligned16(ws) || !aligned16(logits) || ((uintptr_t)logit_stats & 7u)) return KB_ERR_ALIGN;
+    cudaStream_t st = as_stream(stream);
+    Workspace w;
+    layout(d, B, T, reinterpret_cast<char*>(ws), &w);
+    const int C = d.n_embd;
+    const int R = B * T;
+    const size_t BC = (size_t)B * C;
+
+    const bool i8 = d.wdtype == KB_I8;
+    const bool bf = d.wdtype == KB_BF16;
+    const double bpe = 2.0;  // fp16 bytes per activation element
     {
         ProfScope ps(PH_EMBED, st, (double)R * C * 2 * bpe);
         KB_TRY(launch_embed(tokens, R, d.n_vocab, C, d.emb, w.x, st));
     }
-    for (int l = 0; l < d.n_layer; ++l) {
-        const kb_layer_desc& L = d.layers[l];
-        float* s = state + (size_t)l * 5 * BC;
-        float *s_att = s, *s_aa = s + BC, *s_bb = s + 2 * BC, *s_pp = s + 3 * BC,
-              *s_ffn = s + 4 * BC;
-
-        // ---- time mix -------------------------------------------------------
-        MixArgs ma{{L.att_mix_k, L.att_mix_v, L.att_mix_r}, {w.kx, w.vx, w.rx},
-                   {w.q_kx, w.q_vx, w.q_rx}, {w.s_kx, w.s_vx, w.s_rx}, bf ? 1 : 0};
-        {
-            ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? 2 * bpe + 3 : 4 * bpe));
-            KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
-        }
-        if (i8) {
-            KB_TRY(gemm8(w.q_kx, w.s_kx, L.att_kw, L.att_ks, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm8(w.q_vx, w.s_vx, L.att_vw, L.att_vs, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm8(w.q_rx, w.s_rx, L.att_rw, L.att_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-        } else {
-            KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-        }
-        {
-            ProfScope ps(PH_WKV, st, (double)R * C * 12.0);
-            KB_TRY(launch_wkv(d.wkv_convention, B, T, C, w.k, w.v, w.r, L.att_decay, L.att_first,
-                              s_aa, s_bb, s_pp, w.ry, st, bf));
-        }
-        if (i8) {
-            KB_TRY(quant(w.ry, C, w.q_ry, w.s_ry));
-            KB_TRY(gemm8(w.q_ry, w.s_ry, L.att_ow, L.att_os, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
-        } else {
-            KB_TRY(gemm(w.ry, L.att_ow, R, C, C, KB_EPI_RESID, w.x, w.x, nullptr, PH_GEMM));
-        }
-        if (cudaMemcpyAsync(s_att, w.xx_att, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            return launch_status();
-
-        // ---- channel mix ----------------------------------------------------
-        MixArgs mf{{L.ffn_mix_k, L.ffn_mix_r, nullptr}, {w.kx, w.rx, nullptr},
-                   {w.q_kx, w.q_rx, nullptr}, {w.s_kx, w.s_rx, nullptr}, bf ? 1 : 0};
-        {
-            ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? bpe + 2 : 3 * bpe));
-            KB_TRY(launch_ln_mix(2, w.x, B, T, C, L.ln2_w, L.ln2_b, mf, s_ffn, w.xx_ffn, nullptr, st));
-        }
-        if (i8) {
-            KB_TRY(gemm8(w.q_rx, w.s_rx, L.ffn_rw, L.ffn_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm8(w.q_kx, w.s_kx, L.ffn_kw, L.ffn_ks, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
-            KB_TRY(quant(w.kk, F, w.q_kk, w.s_kk));
-            KB_TRY(gemm8(w.q_kk, w.s_kk, L.ffn_vw, L.ffn_vs, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
-        } else {
-            KB_TRY(gemm(w.rx, L.ffn_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm(w.kx, L.ffn_kw, R, F, C, KB_EPI_RELU_SQ, w.kk, nullptr, nullptr, PH_GEMM));
-            KB_TRY(gemm(w.kk, L.ffn_vw, R, C, F, KB_EPI_GATE_RESID, w.x, w.x, w.r, PH_GEMM));
-        }
-        if (cudaMemcpyAsync(s_ffn, w.xx_ffn, BC * 4, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
-            return launch_status();
-    }
+    for (int l = 0; l < d.n_layer; ++l)
+        KB_TRY(run_layer(d, d.layers[l], w, B, T, state + (size_t)l * 5 * BC, st));
     MixArgs none{{nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr},
                  {w.q_kx, nullptr, nullptr}, {w.s_kx, nullptr, nullptr}, bf ? 1 : 0};
     {
@@ -339,6 +355,19 @@ extern "C" int kb_forward_window(const kb_model* m, const int32_t* tokens, int B
         }
     }
     return KB_OK;
+}
+
+extern "C" int kb_layer_forward(const kb_model* m, int layer, uint16_t* x, int B, int T,
+                                float* layer_state, void* ws, size_t ws_bytes, void* stream) {
+    if (!m || !x || !layer_state || !ws || B <= 0 || T <= 0) return KB_ERR_ARG;
+    const kb_model_desc& d = m->d;
+    if (layer < 0 || layer >= d.n_layer) return KB_ERR_ARG;
+    if (ws_bytes < layout(d, B, T, nullptr, nullptr)) return KB_ERR_WORKSPACE;
+    if (!aligned16(ws) || !aligned16(x)) return KB_ERR_ALIGN;
+    Workspace w;
+    layout(d, B, T, reinterpret_cast<char*>(ws), &w);
+    w.x = x;  // the caller's residual rows are read and updated in place
+    return run_layer(d, d.layers[layer], w, B, T, layer_state, as_stream(stream));
 }
 
 // ---------------------------------------------------------------------------

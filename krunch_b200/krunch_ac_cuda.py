@@ -131,3 +131,140 @@ def det_matmul(x: torch.Tensor, W: torch.Tensor, out_dtype=None) -> torch.Tensor
            N.KB_EPI_F32 if f32 else N.KB_EPI_F16, out.data_ptr(), Np, None, None,
            N.stream_ptr(x.device))
     return out[:, :Nn] if Np != Nn else out
+
+
+# --------------------------------------------------------------------------
+# rwkv4_layer_step_cpp / rwkv4_layer_step_cpp_t1 (layer_cpp.cpp:294-307,
+# 456-637): one RWKV-4 layer over x [B, T, C] with the 18 layer tensors in
+# the order of cpp_path.init_weights (cpp_path.py:59-78) — LN and mixes
+# fp16 [C], time_decay / time_first fp32 [C] as the rwkv loader leaves them
+# (time_decay already -exp(raw)), matrices [in, out] fp16 (or bf16).  The
+# layer runs the production WKV convention, as the reference's layer does
+# (rwkv::wkv_forward or its own wkv_kernel.cu:57-72).  State tensors
+# att_xx / ffn_xx [B, C] (fp16), aa / bb / pp [B, C] fp32 are updated in
+# place; the new x is returned.
+# --------------------------------------------------------------------------
+
+class _LayerHandle:
+    """A one-layer kb_model over device copies of the reference's layer
+    tensors in this library's layout (matrices K-major, LN / mixes fp32,
+    decay = -time_decay).  Cached per set of input tensors, like the
+    reference's weight and graph caches (one host thread per process)."""
+
+    def __init__(self, w, dev):
+        import ctypes as C
+        (ln1_w, ln1_b, tm_k, tm_v, tm_r, td, tf, Kw, Vw, Rw, Ow,
+         ln2_w, ln2_b, ftm_k, ftm_r, fKw, fVw, fRw) = w
+        self.keep = []
+        Cm = Kw.shape[0]
+        Fm = fKw.shape[1]
+        bf = Kw.dtype == torch.bfloat16
+        for t, nm in ((Kw, "Kw"), (Vw, "Vw"), (Rw, "Rw"), (Ow, "Ow"), (fKw, "ffn_Kw"),
+                      (fVw, "ffn_Vw"), (fRw, "ffn_Rw")):
+            if t.dtype not in (torch.float16, torch.bfloat16) or t.dtype != Kw.dtype:
+                raise RuntimeError(f"{nm} must be fp16 or bf16 like Kw")
+        if tuple(Kw.shape) != (Cm, Cm) or tuple(fVw.shape) != (Fm, Cm):
+            raise RuntimeError("layer matrices must be [in, out] with n_att == n_embd")
+
+        def f32(t):
+            t = t.detach().reshape(-1).to(dev, torch.float32).contiguous()
+            self.keep.append(t)
+            return t.data_ptr()
+
+        def km(t):
+            t = t.detach().to(dev).t().contiguous()
+            self.keep.append(t)
+            return t.data_ptr()
+
+        d = N.LayerDesc()
+        d.ln1_w, d.ln1_b, d.ln2_w, d.ln2_b = f32(ln1_w), f32(ln1_b), f32(ln2_w), f32(ln2_b)
+        d.att_mix_k, d.att_mix_v, d.att_mix_r = f32(tm_k), f32(tm_v), f32(tm_r)
+        d.att_decay = f32(-td.float())
+        d.att_first = f32(tf)
+        d.att_kw, d.att_vw, d.att_rw, d.att_ow = km(Kw), km(Vw), km(Rw), km(Ow)
+        d.ffn_mix_k, d.ffn_mix_r = f32(ftm_k), f32(ftm_r)
+        d.ffn_kw, d.ffn_vw, d.ffn_rw = km(fKw), km(fVw), km(fRw)
+        self.layers = (N.LayerDesc * 1)(d)
+        # the layer entry never reads the embedding, final LayerNorm or head:
+        # a 128-row placeholder satisfies the model description
+        dummy = torch.zeros((128, Cm), dtype=Kw.dtype, device=dev)
+        ones = torch.ones(Cm, dtype=torch.float32, device=dev)
+        self.keep += [dummy, ones]
+        md = N.ModelDesc()
+        md.n_layer, md.n_embd, md.n_ffn, md.n_vocab, md.vocab_pad = 1, Cm, Fm, 128, 128
+        md.wdtype = N.KB_BF16 if bf else N.KB_F16
+        md.wkv_convention = N.KB_WKV_PRODUCTION
+        md.emb, md.head = dummy.data_ptr(), dummy.data_ptr()
+        md.ln_out_w = md.ln_out_b = ones.data_ptr()
+        md.layers = self.layers
+        md.head_scale = None
+        h = C.c_void_p()
+        N.call("kb_model_create", C.byref(md), C.byref(h))
+        self.handle = h
+        self.C, self.F = Cm, Fm
+        self.ws = None
+
+    def workspace(self, B, T, dev):
+        n = int(N.load().kb_forward_workspace_bytes(self.handle, B, T))
+        if self.ws is None or self.ws.numel() < n:
+            self.ws = torch.empty(n, dtype=torch.uint8, device=dev)
+        return self.ws
+
+    def __del__(self):
+        h = getattr(self, "handle", None)
+        if h is not None and h.value:
+            try:
+                N.load().kb_model_destroy(h)
+            except Exception:
+                pass
+
+
+_LAYER_CACHE: dict = {}
+
+
+def _layer_handle(w, dev) -> _LayerHandle:
+    key = tuple((t.data_ptr(), tuple(t.shape), t.dtype) for t in w)
+    h = _LAYER_CACHE.get(key)
+    if h is None:
+        h = _LAYER_CACHE[key] = _LayerHandle(w, dev)
+    return h
+
+
+def clear_layer_graph_cache() -> None:
+    """Drop the cached layer handles (the reference's cache reset,
+    layer_cpp.cpp:1038)."""
+    _LAYER_CACHE.clear()
+
+
+def rwkv4_layer_step_cpp(x, att_xx, aa, bb, pp, ffn_xx, *layer):
+    if len(layer) != 18:
+        raise RuntimeError(f"expected 18 layer tensors, got {len(layer)}")
+    _chk(x, "x", (torch.float16,))
+    if x.dim() != 3:
+        raise RuntimeError("x must be [B, T, C]")
+    B, T, Cm = x.shape
+    for t, nm in ((aa, "aa"), (bb, "bb"), (pp, "pp")):
+        _chk(t, nm, (torch.float32,))
+    for t, nm in ((att_xx, "att_xx"), (ffn_xx, "ffn_xx")):
+        _chk(t, nm, (torch.float16, torch.bfloat16, torch.float32))
+    for t, nm in zip((att_xx, aa, bb, pp, ffn_xx), ("att_xx", "aa", "bb", "pp", "ffn_xx")):
+        if t.numel() != B * Cm:
+            raise RuntimeError(f"{nm} must hold [B, C] = [{B}, {Cm}]")
+    h = _layer_handle(layer, x.device)
+    if h.C != Cm:
+        raise RuntimeError("x width differs from the layer's n_embd")
+    st = torch.stack([t.reshape(B, Cm).float() for t in (att_xx, aa, bb, pp, ffn_xx)]).contiguous()
+    out = x.reshape(B * T, Cm).clone()
+    ws = h.workspace(B, T, x.device)
+    N.call("kb_layer_forward", h.handle, 0, out.data_ptr(), B, T, st.data_ptr(), ws.data_ptr(),
+           ws.numel(), N.stream_ptr(x.device))
+    for i, t in enumerate((att_xx, aa, bb, pp, ffn_xx)):
+        t.copy_(st[i].view_as(t))
+    return out.view(B, T, Cm)
+
+
+def rwkv4_layer_step_cpp_t1(x, att_xx, aa, bb, pp, ffn_xx, *layer):
+    """The single-token form ([1, 1, C]); the same kernels as any window."""
+    if x.dim() != 3 or x.shape[0] != 1 or x.shape[1] != 1:
+        raise RuntimeError("x must be [1, 1, C]")
+    return rwkv4_layer_step_cpp(x, att_xx, aa, bb, pp, ffn_xx, *layer)
