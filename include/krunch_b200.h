@@ -338,18 +338,19 @@ int kb_step_error_status(int reset);
 
 /* Allocation-free variant of kb_forward_window.  No counterpart in the
  * reference: it exists for hosts that cannot allocate device memory when they
- * run a forward, e.g. a decode loop being recorded into a CUDA graph (device
- * allocation is not allowed during stream capture), a foreign-language host
- * (Go/JNI/Rust over this ABI) whose process runs under a fixed device-memory
- * budget handed out at start-up, or a caller without a CUDA allocator of its
- * own.  The caller still passes tokens, state and logits; the activation
- * workspace lives in a file-scope __device__ array of
- * KB_NOALLOC_SCRATCH_BYTES that every GPU loading this library keeps until
- * process exit.
+ * run a forward, e.g. a foreign-language host (Go/JNI/Rust over this ABI)
+ * whose process runs under a fixed device-memory budget handed out at
+ * start-up, or a caller without a CUDA allocator of its own.  The caller
+ * still passes tokens, state and logits; the activation workspace lives in a
+ * file-scope __device__ array of KB_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading this library keeps until process exit.
  *   - The first call on a device resolves that array's device address (with
  *     the device current), so make it before any stream capture begins.
  *   - Windows whose workspace (kb_forward_workspace_bytes) exceeds the array
- *     return KB_ERR_TOO_LARGE; 8 MiB covers B*T <= 384 rows of RWKV-4-169M.
+ *     return KB_ERR_TOO_LARGE.  At RWKV-4-169M the 8 MiB hold one stream of
+ *     up to 389 tokens or up to 303 streams of one token with fp16 / bf16
+ *     weights, and 302 tokens or 248 streams with int8 weights; ask
+ *     kb_forward_workspace_bytes for other shapes.
  *   - All calls share the one array and it keeps the previous call's
  *     contents; nothing in it needs to start at zero.  Calls that can overlap
  *     on the GPU (other streams, other host threads) race on it: serialise

@@ -1,6 +1,6 @@
 """kb_forward_window_noalloc: the forward for callers that cannot allocate
-device memory (a decode loop recorded into a CUDA graph, or a foreign host
-under a fixed device-memory budget).  Its activations live in the library's
+device memory (a foreign host under a fixed device-memory budget, or a
+caller without a CUDA allocator of its own).  Its activations live in the library's
 fixed device array instead of a caller workspace; its output must equal the
 regular entry point's.
 
