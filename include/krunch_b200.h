@@ -200,6 +200,21 @@ int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int8_t*
                void* out, int64_t ldo, const uint16_t* resid, const uint16_t* gate,
                int tile_n, void* stream);
 
+/* The three attention projections of a layer in ONE launch over a shared
+ * tile space: k = kx @ Kw^T (fp32), v = vx @ Vw^T (fp32),
+ * r = sigmoid(rx @ Rw^T) (fp16), all [M, N] with row stride ldo.  dtype
+ * KB_F16 / KB_BF16 (scales NULL) or KB_I8 (per-row A factors, per-output
+ * channel W factors as in kb_gemm_i8).  Each output element has the bits of
+ * the corresponding single kb_gemm / kb_gemm_i8 call.  Replaces
+ * det_matmul_tc_3way_async (krunch_ac/cuda/det_matmul_tc_3way_async.cu:50-251,
+ * routed at layer_cpp.cpp:531-556). */
+int kb_gemm_kvr(int dtype, const void* kx, const void* vx, const void* rx, int64_t lda,
+                const float* kx_scale, const float* vx_scale, const float* rx_scale,
+                const void* kw, const void* vw, const void* rw, int64_t ldw,
+                const uint16_t* kw_scale, const uint16_t* vw_scale, const uint16_t* rw_scale,
+                int M, int N, int K, float* k, float* v, uint16_t* r, int64_t ldo, int tile_n,
+                void* stream);
+
 /* Per-output-channel int8 weight quantisation of fp16 W [N, K]:
  * scale[n] = fp16(max_k |W[n,k]| / 127), q = clamp(rint(W / scale), -127, 127). */
 int kb_quantize_weight(const uint16_t* w, int N, int K, int8_t* q, uint16_t* scale,
@@ -320,10 +335,13 @@ size_t kb_step_workspace_bytes(const kb_model* model, int B);
 int kb_step_forward(kb_model* model, const int32_t* tokens, int B, float* state,
                     void* workspace, size_t workspace_bytes, uint16_t* logits,
                     float* logit_stats, void* stream);
-/* Profiling aid: a device buffer of >= 1024 u64 receives, for CTA 0 of each
+/* Profiling aid: a device buffer of >= 2048 u64 receives, for CTA 0 of each
  * later kb_step_forward, %globaltimer at every grid barrier's entry (slot
- * 2e) and exit (slot 2e+1), and per tile phase tp the times its first unit's
- * loads were issued, landed, multiplied and stored (slots 512 + 4 tp ..);
+ * 2e) and exit (slot 2e+1), per tile phase tp the SM clocks when its first
+ * unit's loads were issued, landed, multiplied and stored (slots
+ * 512 + 4 tp ..), the SM clock at each barrier exit (768 + e), and per row
+ * phase rp the SM clocks of row 0 at entry, data consumed, row reduction
+ * done and end (1024 + 4 rp ..);
  * NULL turns it off. */
 int kb_step_set_trace(unsigned long long* trace);
 /* Failure-detection test hook of the fused step: withhold != 0 makes CTA 0

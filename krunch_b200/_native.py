@@ -69,6 +69,8 @@ SIGNATURES = {
     "kb_step_set_trace": (i32, [vp]),
     "kb_step_set_fault": (i32, [i32, i64]),
     "kb_gemm_i8": (i32, [vp, i64, vp, vp, i64, vp, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),
+    "kb_gemm_kvr": (i32, [i32, vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, i64, vp, vp, vp, i32, i32,
+                          i32, vp, vp, vp, i64, i32, vp]),
     "kb_quantize_weight": (i32, [vp, i32, i32, vp, vp, vp]),
     "kb_quantize_rows": (i32, [vp, i32, i32, vp, vp, vp]),
     "kb_gemm_tiled": (i32, [i32, vp, i64, vp, i64, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp]),

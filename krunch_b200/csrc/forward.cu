@@ -244,14 +244,16 @@ int run_layer(const kb_model_desc& d, const kb_layer_desc& L, const Workspace& w
         ProfScope ps(PH_LN_MIX, st, (double)R * C * (i8 ? 2 * bpe + 3 : 4 * bpe));
         KB_TRY(launch_ln_mix(3, w.x, B, T, C, L.ln1_w, L.ln1_b, ma, s_att, w.xx_att, nullptr, st));
     }
-    if (i8) {
-        KB_TRY(gemm8(w.q_kx, w.s_kx, L.att_kw, L.att_ks, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm8(w.q_vx, w.s_vx, L.att_vw, L.att_vs, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm8(w.q_rx, w.s_rx, L.att_rw, L.att_rs, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
-    } else {
-        KB_TRY(gemm(w.kx, L.att_kw, R, C, C, KB_EPI_F32, w.k, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.vx, L.att_vw, R, C, C, KB_EPI_F32, w.v, nullptr, nullptr, PH_GEMM));
-        KB_TRY(gemm(w.rx, L.att_rw, R, C, C, KB_EPI_SIGMOID, w.r, nullptr, nullptr, PH_GEMM));
+    {
+        // k, v, r projections in one launch (the reference's 3-way kernel)
+        ProfScope ps(PH_GEMM, st, 3.0 * 2.0 * R * (double)C * C);
+        const void* const A[3] = {i8 ? (const void*)w.q_kx : w.kx, i8 ? (const void*)w.q_vx : w.vx,
+                                  i8 ? (const void*)w.q_rx : w.rx};
+        const float* const as[3] = {w.s_kx, w.s_vx, w.s_rx};
+        const void* const W[3] = {L.att_kw, L.att_vw, L.att_rw};
+        const uint16_t* const ws[3] = {L.att_ks, L.att_vs, L.att_rs};
+        void* const out[3] = {w.k, w.v, w.r};
+        KB_TRY(launch_gemm_kvr(d.wdtype, A, C, as, W, C, ws, R, C, C, out, C, st));
     }
     {
         ProfScope ps(PH_WKV, st, (double)R * C * 12.0);

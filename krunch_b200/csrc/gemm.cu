@@ -59,6 +59,39 @@ extern "C" int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, co
                           gate, as_stream(stream), tile_n);
 }
 
+extern "C" int kb_gemm_kvr(int dtype, const void* kx, const void* vx, const void* rx, int64_t lda,
+                           const float* kx_scale, const float* vx_scale, const float* rx_scale,
+                           const void* kw, const void* vw, const void* rw, int64_t ldw,
+                           const uint16_t* kw_scale, const uint16_t* vw_scale,
+                           const uint16_t* rw_scale, int M, int N, int K, float* k, float* v,
+                           uint16_t* r, int64_t ldo, int tile_n, void* stream) {
+    using namespace kb;
+    if (!kx || !vx || !rx || !kw || !vw || !rw || !k || !v || !r || M < 0 || N <= 0 || K <= 0)
+        return KB_ERR_ARG;
+    if (tile_n != 0 && tile_n != 32 && tile_n != 64 && tile_n != 128 && tile_n != 256 &&
+        tile_n != KB_TILE_PAIR)
+        return KB_ERR_ARG;
+    if (dtype != KB_F16 && dtype != KB_BF16 && dtype != KB_I8) return KB_ERR_UNSUPPORTED;
+    const bool i8 = dtype == KB_I8;
+    if (i8 && (!kx_scale || !vx_scale || !rx_scale || !kw_scale || !vw_scale || !rw_scale))
+        return KB_ERR_ARG;
+    if (N % 32 || K % (i8 ? 128 : 64)) return KB_ERR_SHAPE;
+    const int el = i8 ? 16 : 8;  // elements per 16 bytes of A / W
+    const void* ptrs[9] = {kx, vx, rx, kw, vw, rw, k, v, r};
+    for (const void* q : ptrs)
+        if (!aligned16(q)) return KB_ERR_ALIGN;
+    if (i8 && (!aligned16(kw_scale) || !aligned16(vw_scale) || !aligned16(rw_scale)))
+        return KB_ERR_ALIGN;
+    if ((lda % el) || (ldw % el) || lda < K || ldw < K || ldo < N || (ldo % 8)) return KB_ERR_ALIGN;
+    const void* const A[3] = {kx, vx, rx};
+    const void* const W[3] = {kw, vw, rw};
+    const float* const as[3] = {kx_scale, vx_scale, rx_scale};
+    const uint16_t* const ws[3] = {kw_scale, vw_scale, rw_scale};
+    void* const out[3] = {k, v, r};
+    return launch_gemm_kvr(dtype, A, lda, as, W, ldw, ws, M, N, K, out, ldo, as_stream(stream),
+                           tile_n);
+}
+
 extern "C" int kb_device_error_status(int reset) {
     const int e = kb::read_tc_error(reset);
     if (e < 0) return KB_ERR_CUDA;

@@ -94,9 +94,21 @@ struct TcArgs {
     int V;                    // head: valid vocabulary columns
     float2* stats;            // head: subtile partials
     int stats_stride;
-    const float* a_scale;     // int8: dequantisation factor per row of A
-    const uint16_t* w_scale;  // int8: fp16 dequantisation factor per row of W
+    const float* a_scale[3];     // int8: dequantisation factor per row of A (per GEMM)
+    const uint16_t* w_scale[3];  // int8: fp16 dequantisation factor per row of W (per GEMM)
 };
+
+// Tensor maps of a launch: A, W and output per GEMM.  One GEMM uses entry 0;
+// the grouped k/v/r launch (TC_EPI_KVR) runs three GEMMs of the same shape
+// over one tile space.
+struct TcMaps {
+    CUtensorMap a[3], b[3], o[3];
+};
+
+// Internal epilogue id of the grouped k/v/r launch: GEMMs 0 and 1 store
+// fp32 (KB_EPI_F32: k and v), GEMM 2 stores fp16 sigmoid (KB_EPI_SIGMOID: r),
+// as the reference's 3-way kernel does (det_matmul_tc_3way_async.cu:50-251).
+constexpr int TC_EPI_KVR = 7;
 
 __device__ int g_tc_error = 0;
 
@@ -277,11 +289,51 @@ __device__ __forceinline__ void dequant32(uint32_t (&v)[32], float sa, const uin
     }
 }
 
+// Non-head epilogue of one tile: this warp's 32-column chunks [c_lo, c_hi)
+// of TMEM lane quadrant q, epilogue E, stored through mapO.
+template <int E, int KIND>
+__device__ __forceinline__ void epi_chunks(int c_lo, int c_hi, int n0, int N, int M, int m0,
+                                           int q, int lane, uint32_t tbase, float sa,
+                                           const uint16_t* w_scale, const CUtensorMap* mapO,
+                                           const TcArgs& args, int64_t ldo, unsigned char* ring,
+                                           uint32_t& nst) {
+#pragma unroll 1
+    for (int c = c_lo; c < c_hi; ++c) {
+        const int col0 = n0 + c * 32;
+        if (col0 >= N) break;
+        uint32_t v[32];
+        tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
+        tc::tmem_ld_wait();
+        if (KIND == TC_I8) dequant32(v, sa, w_scale + col0);
+        if (E == KB_EPI_F32) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // two 16-column (64-byte) halves
+                uint32_t w[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) w[j] = v[16 * h + j];
+                stage_and_store(out_tile(ring, nst, lane), lane, w, mapO,
+                                col0 + 16 * h, m0 + q * 32);
+            }
+        } else {
+            uint32_t w[16];
+            uint4 rv[4], gv[4];
+            unsigned char* const st = out_tile(ring, nst, lane);
+            if (E == KB_EPI_RESID || E == KB_EPI_GATE_RESID)
+                load_tile_rows(args.resid, ldo, m0 + q * 32, col0, M, st, lane, rv);
+            if (E == KB_EPI_GATE_RESID)
+                load_tile_rows(args.gate, ldo, m0 + q * 32, col0, M, st, lane, gv);
+            // a bf16 model's relu(k)^2 is the next GEMM's bf16 operand
+            tc_epi_pack<E, KIND == TC_BF16 && E == KB_EPI_RELU_SQ>(v, rv, gv, w);
+            stage_and_store(st, lane, w, mapO, col0, m0 + q * 32);
+        }
+    }
+}
+
 template <int EPI, int BN, int KIND, bool PAIR>
 __global__ void __launch_bounds__(TC_NT, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-              const __grid_constant__ CUtensorMap mapO, const __grid_constant__ TcArgs args) {
+    k_gemm_tc(const __grid_constant__ TcMaps maps, const __grid_constant__ TcArgs args) {
     using Cfg = TcCfg<BN, KIND, PAIR>;
+    constexpr int G = EPI == TC_EPI_KVR ? 3 : 1;  // GEMMs sharing the tile space
     const int M = args.M, N = args.N, K = args.K;
     const int64_t ldo = args.ldo;
     const int V = args.V, stats_stride = args.stats_stride;
@@ -297,7 +349,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_n = (N + BN - 1) / BN;
     const int num_m = (M + Cfg::BM - 1) / Cfg::BM;
-    const int tiles = num_m * num_n;
+    const int tiles = num_m * num_n * G;  // tile t: GEMM t % G, position t / G
     const int KB = K / Cfg::KEL;
     // a pair walks the tiles as one unit; rank 1 holds rows 128..255 of each
     const uint32_t rank = PAIR ? tc::cluster_ctarank() : 0u;
@@ -317,9 +369,11 @@ __global__ void __launch_bounds__(TC_NT, 1)
         tc::fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
-        tc::prefetch_tmap(&mapA);
-        tc::prefetch_tmap(&mapB);
-        tc::prefetch_tmap(&mapO);
+        for (int g = 0; g < G; ++g) {
+            tc::prefetch_tmap(&maps.a[g]);
+            tc::prefetch_tmap(&maps.b[g]);
+            tc::prefetch_tmap(&maps.o[g]);
+        }
     }
     if (warp == 1) {
         if (PAIR) tc::tmem_alloc_pair(&bars->tmem_base, Cfg::TMEM_COLS);
@@ -342,7 +396,10 @@ __global__ void __launch_bounds__(TC_NT, 1)
 #endif
             for (int t = unit0; t < tiles && !tc_aborted(bars); t += units) {
                 int m0, n0;
-                tile_coords<BN, Cfg::BM>(t, num_m, num_n, m0, n0);
+                const int g = t % G;
+                tile_coords<BN, Cfg::BM>(t / G, num_m, num_n, m0, n0);
+                const CUtensorMap* mapA = &maps.a[g];
+                const CUtensorMap* mapB = &maps.b[g];
                 for (int kb = 0; kb < KB; ++kb) {
                     DIAG_T0(tw);
                     const bool okw = tc::mbar_wait(&bars->empty[stage], phase ^ 1u);
@@ -356,13 +413,13 @@ __global__ void __launch_bounds__(TC_NT, 1)
                         // both CTAs' bytes complete on the leader's barrier
                         const uint32_t fb = tc::mapa_shared(tc::smem_addr(&bars->full[stage]), 0);
                         if (rank == 0) tc::mbar_expect_tx(&bars->full[stage], 2 * TC_STAGE_BYTES);
-                        tc::tma_load_2d_pair(sa, &mapA, fb, kb * Cfg::KEL, m0 + (int)rank * TC_BM);
-                        tc::tma_load_2d_pair(sa + TC_A_BYTES, &mapB, fb, kb * Cfg::KEL,
+                        tc::tma_load_2d_pair(sa, mapA, fb, kb * Cfg::KEL, m0 + (int)rank * TC_BM);
+                        tc::tma_load_2d_pair(sa + TC_A_BYTES, mapB, fb, kb * Cfg::KEL,
                                              n0 + (int)rank * Cfg::B_ROWS);
                     } else {
                         tc::mbar_expect_tx(&bars->full[stage], TC_STAGE_BYTES);
-                        tc::tma_load_2d(sa, &mapA, &bars->full[stage], kb * Cfg::KEL, m0);
-                        tc::tma_load_2d(sa + TC_A_BYTES, &mapB, &bars->full[stage], kb * Cfg::KEL,
+                        tc::tma_load_2d(sa, mapA, &bars->full[stage], kb * Cfg::KEL, m0);
+                        tc::tma_load_2d(sa + TC_A_BYTES, mapB, &bars->full[stage], kb * Cfg::KEL,
                                         n0);
                     }
                     issued |= 1u << stage;
@@ -472,7 +529,8 @@ __global__ void __launch_bounds__(TC_NT, 1)
             const int a = i & 1;
             const uint32_t use = (uint32_t)(i >> 1);
             int mt, n0;
-            tile_coords<BN, Cfg::BM>(t, num_m, num_n, mt, n0);
+            const int gi = t % G;  // GEMM of this tile
+            tile_coords<BN, Cfg::BM>(t / G, num_m, num_n, mt, n0);
             const int m0 = mt + (int)rank * TC_BM;  // this CTA's 128 rows
             DIAG_T0(tw);
             const bool okt = tc::mbar_wait(&bars->tfull[a], use & 1u);
@@ -484,7 +542,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
             }
             tc::fence_after_sync();
             const int64_t row = m0 + q * 32 + lane;
-            const float sa = (KIND == TC_I8 && row < M) ? args.a_scale[row] : 0.0f;
+            const float sa = (KIND == TC_I8 && row < M) ? args.a_scale[gi][row] : 0.0f;
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
             // 32-column chunks [c_lo, c_hi) of this warp
             constexpr int NCH = BN / 32;
@@ -500,7 +558,7 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     uint32_t v[32];
                     tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
                     tc::tmem_ld_wait();
-                    if (KIND == TC_I8) dequant32(v, sa, args.w_scale + col0);
+                    if (KIND == TC_I8) dequant32(v, sa, args.w_scale[0] + col0);
                     float xr[32];
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
@@ -546,44 +604,25 @@ __global__ void __launch_bounds__(TC_NT, 1)
                             packed[j / 2] = (uint32_t)e0 | ((uint32_t)e1 << 16);
                         }
                     }
-                    stage_and_store(out_tile(ring, nst, lane), lane, packed, &mapO, col0,
+                    stage_and_store(out_tile(ring, nst, lane), lane, packed, &maps.o[0], col0,
                                     m0 + q * 32);
                     if (row < M) {
                         const int u = col0 / SUBTILE;
                         if (u < stats_stride) stats[row * stats_stride + u] = make_float2(m, s);
                     }
                 }
+            } else if (EPI == TC_EPI_KVR) {
+                if (gi < 2)
+                    epi_chunks<KB_EPI_F32, KIND>(c_lo, c_hi, n0, N, M, m0, q, lane, tbase, sa,
+                                                 args.w_scale[gi], &maps.o[gi], args, ldo, ring,
+                                                 nst);
+                else
+                    epi_chunks<KB_EPI_SIGMOID, KIND>(c_lo, c_hi, n0, N, M, m0, q, lane, tbase, sa,
+                                                     args.w_scale[gi], &maps.o[gi], args, ldo,
+                                                     ring, nst);
             } else {
-#pragma unroll 1
-                for (int c = c_lo; c < c_hi; ++c) {
-                    const int col0 = n0 + c * 32;
-                    if (col0 >= N) break;
-                    uint32_t v[32];
-                    tc::tmem_ld32(tbase + (uint32_t)(c * 32), v);
-                    tc::tmem_ld_wait();
-                    if (KIND == TC_I8) dequant32(v, sa, args.w_scale + col0);
-                    if (EPI == KB_EPI_F32) {
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {  // two 16-column (64-byte) halves
-                            uint32_t w[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) w[j] = v[16 * h + j];
-                            stage_and_store(out_tile(ring, nst, lane), lane, w, &mapO,
-                                            col0 + 16 * h, m0 + q * 32);
-                        }
-                    } else {
-                        uint32_t w[16];
-                        uint4 rv[4], gv[4];
-                        unsigned char* const st = out_tile(ring, nst, lane);
-                        if (EPI == KB_EPI_RESID || EPI == KB_EPI_GATE_RESID)
-                            load_tile_rows(args.resid, ldo, m0 + q * 32, col0, M, st, lane, rv);
-                        if (EPI == KB_EPI_GATE_RESID)
-                            load_tile_rows(args.gate, ldo, m0 + q * 32, col0, M, st, lane, gv);
-                        // a bf16 model's relu(k)^2 is the next GEMM's bf16 operand
-                        tc_epi_pack<EPI, KIND == TC_BF16 && EPI == KB_EPI_RELU_SQ>(v, rv, gv, w);
-                        stage_and_store(st, lane, w, &mapO, col0, m0 + q * 32);
-                    }
-                }
+                epi_chunks<EPI, KIND>(c_lo, c_hi, n0, N, M, m0, q, lane, tbase, sa, args.w_scale[0],
+                                      &maps.o[0], args, ldo, ring, nst);
             }
             tc::fence_before_sync();
             __syncwarp();
@@ -702,9 +741,10 @@ int pair_clusters(Kern kern, size_t smem, std::atomic<int>* cache) {
 }
 
 template <int EPI, int BN, int KIND, bool PAIR>
-int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs& args,
-                 cudaStream_t st) {
+int launch_tc_bn(TcMaps& maps, const void* const* W, int64_t ldw, void* const* outs,
+                 const TcArgs& args, cudaStream_t st) {
     using Cfg = TcCfg<BN, KIND, PAIR>;
+    constexpr int G = EPI == TC_EPI_KVR ? 3 : 1;
     static std::atomic<unsigned long long> done{0};
     const cudaError_t attr_err = once_per_device(done, [] {
         return cudaFuncSetAttribute(k_gemm_tc<EPI, BN, KIND, PAIR>,
@@ -714,14 +754,16 @@ int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs
         set_cuda_error(attr_err);
         return KB_ERR_CUDA;
     }
-    CUtensorMap mb, mo;
-    if (!make_map(&mb, W, args.N, args.K, ldw, Cfg::B_ROWS, KIND == TC_I8 ? 1 : 2) ||
-        !make_out_map(&mo, args.out, args.M, args.N, args.ldo, EPI == KB_EPI_F32 ? 4 : 2))
-        return KB_ERR_UNSUPPORTED;
-    const int tiles = ((args.M + Cfg::BM - 1) / Cfg::BM) * ((args.N + BN - 1) / BN);
+    for (int g = 0; g < G; ++g) {
+        const bool f32 = EPI == KB_EPI_F32 || (EPI == TC_EPI_KVR && g < 2);
+        if (!make_map(&maps.b[g], W[g], args.N, args.K, ldw, Cfg::B_ROWS, KIND == TC_I8 ? 1 : 2) ||
+            !make_out_map(&maps.o[g], outs[g], args.M, args.N, args.ldo, f32 ? 4 : 2))
+            return KB_ERR_UNSUPPORTED;
+    }
+    const int tiles = ((args.M + Cfg::BM - 1) / Cfg::BM) * ((args.N + BN - 1) / BN) * G;
     if constexpr (!PAIR) {
         const int grid = tiles < sm_count() ? tiles : sm_count();
-        k_gemm_tc<EPI, BN, KIND, false><<<grid, TC_NT, Cfg::SMEM, st>>>(ma, mb, mo, args);
+        k_gemm_tc<EPI, BN, KIND, false><<<grid, TC_NT, Cfg::SMEM, st>>>(maps, args);
         return launch_status();
     } else {
     static std::atomic<int> clusters[64];
@@ -739,7 +781,7 @@ int launch_tc_bn(const CUtensorMap& ma, const void* W, int64_t ldw, const TcArgs
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, BN, KIND, true>, ma, mb, mo, args);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_gemm_tc<EPI, BN, KIND, true>, maps, args);
     if (e != cudaSuccess) {
         set_cuda_error(e);
         return KB_ERR_CUDA;
@@ -769,23 +811,26 @@ int pick_tile(int M, int N, bool logits) {
     return bn;
 }
 
+// A / W / outs: one pointer per GEMM of the launch (three for TC_EPI_KVR).
 template <int EPI, int KIND>
-int launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, const TcArgs& args,
-              cudaStream_t st, int bn) {
-    CUtensorMap ma;
-    if (!make_map(&ma, A, args.M, args.K, lda, TC_BM, KIND == TC_I8 ? 1 : 2))
-        return KB_ERR_UNSUPPORTED;
-    if (bn == 0) bn = pick_tile(args.M, args.N, EPI == KB_EPI_LOGITS_STATS);
+int launch_tc(const void* const* A, int64_t lda, const void* const* W, int64_t ldw,
+              void* const* outs, const TcArgs& args, cudaStream_t st, int bn) {
+    constexpr int G = EPI == TC_EPI_KVR ? 3 : 1;
+    TcMaps maps;
+    for (int g = 0; g < G; ++g)
+        if (!make_map(&maps.a[g], A[g], args.M, args.K, lda, TC_BM, KIND == TC_I8 ? 1 : 2))
+            return KB_ERR_UNSUPPORTED;
+    if (bn == 0) bn = pick_tile(args.M, args.N * G, EPI == KB_EPI_LOGITS_STATS);
     switch (bn) {
         case KB_TILE_PAIR: {
-            const int r = launch_tc_bn<EPI, 256, KIND, true>(ma, W, ldw, args, st);
+            const int r = launch_tc_bn<EPI, 256, KIND, true>(maps, W, ldw, outs, args, st);
             if (r != KB_ERR_UNSUPPORTED) return r;
-            return launch_tc_bn<EPI, 256, KIND, false>(ma, W, ldw, args, st);
+            return launch_tc_bn<EPI, 256, KIND, false>(maps, W, ldw, outs, args, st);
         }
-        case 256: return launch_tc_bn<EPI, 256, KIND, false>(ma, W, ldw, args, st);
-        case 128: return launch_tc_bn<EPI, 128, KIND, false>(ma, W, ldw, args, st);
-        case 64: return launch_tc_bn<EPI, 64, KIND, false>(ma, W, ldw, args, st);
-        case 32: return launch_tc_bn<EPI, 32, KIND, false>(ma, W, ldw, args, st);
+        case 256: return launch_tc_bn<EPI, 256, KIND, false>(maps, W, ldw, outs, args, st);
+        case 128: return launch_tc_bn<EPI, 128, KIND, false>(maps, W, ldw, outs, args, st);
+        case 64: return launch_tc_bn<EPI, 64, KIND, false>(maps, W, ldw, outs, args, st);
+        case 32: return launch_tc_bn<EPI, 32, KIND, false>(maps, W, ldw, outs, args, st);
         default: return KB_ERR_ARG;
     }
 }
@@ -793,14 +838,17 @@ int launch_tc(const void* A, int64_t lda, const void* W, int64_t ldw, const TcAr
 template <int KIND>
 int launch_epi(const void* A, int64_t lda, const void* W, int64_t ldw, int epi,
                const TcArgs& args, cudaStream_t st, int bn) {
+    const void* const a[1] = {A};
+    const void* const w[1] = {W};
+    void* const o[1] = {args.out};
     switch (epi) {
-        case KB_EPI_F32: return launch_tc<KB_EPI_F32, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_F16: return launch_tc<KB_EPI_F16, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_SIGMOID: return launch_tc<KB_EPI_SIGMOID, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_RELU_SQ: return launch_tc<KB_EPI_RELU_SQ, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_RESID: return launch_tc<KB_EPI_RESID, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID, KIND>(A, lda, W, ldw, args, st, bn);
-        case KB_EPI_LOGITS_STATS: return launch_tc<KB_EPI_LOGITS_STATS, KIND>(A, lda, W, ldw, args, st, bn);
+        case KB_EPI_F32: return launch_tc<KB_EPI_F32, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_F16: return launch_tc<KB_EPI_F16, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_SIGMOID: return launch_tc<KB_EPI_SIGMOID, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_RELU_SQ: return launch_tc<KB_EPI_RELU_SQ, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_RESID: return launch_tc<KB_EPI_RESID, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_GATE_RESID: return launch_tc<KB_EPI_GATE_RESID, KIND>(a, lda, w, ldw, o, args, st, bn);
+        case KB_EPI_LOGITS_STATS: return launch_tc<KB_EPI_LOGITS_STATS, KIND>(a, lda, w, ldw, o, args, st, bn);
         default: return KB_ERR_ARG;
     }
 }
@@ -812,7 +860,7 @@ int launch_gemm_tc(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ld
                    const uint16_t* gate, cudaStream_t st, int bn) {
     if (M == 0) return KB_OK;
     if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
-    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, nullptr, nullptr};
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, {}, {}};
     return launch_epi<TC_F16>(A, lda, W, ldw, epi, args, st, bn);
 }
 
@@ -821,7 +869,7 @@ int launch_gemm_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t 
                      const uint16_t* gate, cudaStream_t st, int bn) {
     if (M == 0) return KB_OK;
     if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
-    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, nullptr, nullptr};
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, {}, {}};
     return launch_epi<TC_BF16>(A, lda, W, ldw, epi, args, st, bn);
 }
 
@@ -830,7 +878,7 @@ int launch_gemm_logits_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, i
                             int stats_stride, cudaStream_t st) {
     if (M == 0) return KB_OK;
     const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
-                      stats_stride, nullptr, nullptr};
+                      stats_stride, {}, {}};
     return launch_epi<TC_BF16>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
 }
 
@@ -840,7 +888,7 @@ int launch_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, const int
                    int bn) {
     if (M == 0) return KB_OK;
     if (epi == KB_EPI_LOGITS_STATS) return KB_ERR_ARG;
-    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, a_scale, w_scale};
+    const TcArgs args{M, N, K, out, ldo, resid, gate, 0, nullptr, 0, {a_scale}, {w_scale}};
     return launch_epi<TC_I8>(A, lda, W, ldw, epi, args, st, bn);
 }
 
@@ -849,7 +897,7 @@ int launch_gemm_logits(const uint16_t* A, int64_t lda, const uint16_t* W, int64_
                        int stats_stride, cudaStream_t st) {
     if (M == 0) return KB_OK;
     const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
-                      stats_stride, nullptr, nullptr};
+                      stats_stride, {}, {}};
     return launch_epi<TC_F16>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
 }
 
@@ -859,8 +907,25 @@ int launch_gemm_logits_i8(const int8_t* A, int64_t lda, const float* a_scale, co
                           cudaStream_t st) {
     if (M == 0) return KB_OK;
     const TcArgs args{M, N, K, out, ldo, nullptr, nullptr, V, reinterpret_cast<float2*>(stats),
-                      stats_stride, a_scale, w_scale};
+                      stats_stride, {a_scale}, {w_scale}};
     return launch_epi<TC_I8>(A, lda, W, ldw, KB_EPI_LOGITS_STATS, args, st, 0);
+}
+
+// k = kx @ Kw^T (fp32), v = vx @ Vw^T (fp32), r = sigmoid(rx @ Rw^T) (fp16)
+// in one launch; same shapes, same bits as three launch_gemm_* calls.
+int launch_gemm_kvr(int kind, const void* const (&A)[3], int64_t lda,
+                    const float* const (&a_scale)[3], const void* const (&W)[3], int64_t ldw,
+                    const uint16_t* const (&w_scale)[3], int M, int N, int K,
+                    void* const (&out)[3], int64_t ldo, cudaStream_t st, int bn) {
+    if (M == 0) return KB_OK;
+    TcArgs args{M, N, K, nullptr, ldo, nullptr, nullptr, 0, nullptr, 0,
+                {a_scale[0], a_scale[1], a_scale[2]}, {w_scale[0], w_scale[1], w_scale[2]}};
+    switch (kind) {
+        case KB_F16: return launch_tc<TC_EPI_KVR, TC_F16>(A, lda, W, ldw, out, args, st, bn);
+        case KB_BF16: return launch_tc<TC_EPI_KVR, TC_BF16>(A, lda, W, ldw, out, args, st, bn);
+        case KB_I8: return launch_tc<TC_EPI_KVR, TC_I8>(A, lda, W, ldw, out, args, st, bn);
+        default: return KB_ERR_ARG;
+    }
 }
 
 int read_tc_error(int reset) {

@@ -58,6 +58,14 @@ int launch_gemm_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t 
 int launch_gemm_logits_bf16(const uint16_t* A, int64_t lda, const uint16_t* W, int64_t ldw,
                             int M, int N, int K, uint16_t* out, int64_t ldo, int V, float* stats,
                             int stats_stride, cudaStream_t st);
+// The three attention projections of a layer in one launch: out[0] = fp32
+// A[0] @ W[0]^T, out[1] = fp32 A[1] @ W[1]^T, out[2] = fp16 sigmoid(A[2] @
+// W[2]^T); kind KB_F16 / KB_BF16 / KB_I8 (a_scale / w_scale used for KB_I8
+// only).  Bit-identical to three single launches.
+int launch_gemm_kvr(int kind, const void* const (&A)[3], int64_t lda,
+                    const float* const (&a_scale)[3], const void* const (&W)[3], int64_t ldw,
+                    const uint16_t* const (&w_scale)[3], int M, int N, int K,
+                    void* const (&out)[3], int64_t ldo, cudaStream_t st, int tile_n = 0);
 // Row-wise symmetric int8 quantisation of fp16 [R, K] (quant.cuh).
 int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, cudaStream_t st);
 // Device-side error code of the tcgen05 kernels (0 = none); optionally reset.

@@ -43,6 +43,16 @@
 
 namespace kb {
 
+#ifndef SF_PREISSUE
+#define SF_PREISSUE 0
+#endif
+#ifndef SF_PREROW
+#define SF_PREROW 0
+#endif
+#ifndef SF_NI
+#define SF_NI
+#endif
+
 constexpr int SF_NT = 256;                       // 8 warps
 constexpr int SF_BN = 64;                        // N columns per unit
 constexpr int SF_MAX_KB = 6;                     // 128-byte K blocks per unit
@@ -56,6 +66,7 @@ constexpr size_t SF_ROW_OFF = SF_A_BYTES + 2 * SF_W_BYTES + 256;
 constexpr uint32_t SF_IDESC = tc::idesc_i8(128, SF_BN);
 constexpr int SF_TRACE_TILE = 512;  // + 4 tp: SM clock of CTA 0's first unit
 constexpr int SF_TRACE_CLK = 768;   // + epoch: SM clock at barrier exit
+constexpr int SF_TRACE_ARR = 2048;  // + epoch * grid + cta: %globaltimer at each CTA's arrival
 constexpr unsigned long long SF_SPIN_NS = 2000000000ull;  // grid-barrier wait bound: 2 s
 
 // GEMMs of a layer, in weight-map order
@@ -96,7 +107,8 @@ struct SfParams {
     SfHot h;
 };
 
-constexpr size_t SF_HOT_OFF = SF_ROW_OFF + 2 * (SF_MAX_C + 8) * 4;
+constexpr int SF_RED = 24;  // per-group reduction scratch (floats)
+constexpr size_t SF_HOT_OFF = SF_ROW_OFF + 2 * (SF_MAX_C + SF_RED) * 4;
 constexpr size_t SF_SMEM = SF_HOT_OFF + sizeof(SfHot) + 1024 /*align*/;
 static_assert(SF_SMEM <= 232448, "shared memory per block");
 
@@ -128,44 +140,6 @@ __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
-}
-
-__device__ bool grid_sync(const SfHot& p, SfBars* sb, unsigned epoch) {
-    __syncthreads();
-    if (threadIdx.x == 0 && blockIdx.x == 0 && p.trace) p.trace[2 * epoch] = gtimer();
-    if (threadIdx.x == 0) {
-        // release: the CTA's writes (ordered before this thread by the
-        // __syncthreads above) become visible with the arrival; the proxy
-        // fences order them with the TMA reads of the next tile phase
-        fence_proxy_async_global();
-        if (!(p.withhold_arrival && epoch == 1 && blockIdx.x == 0))
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
-        const unsigned target = epoch * gridDim.x;
-        int ok = 1;
-        const unsigned long long t0 = gtimer();
-        for (uint32_t it = 0;; ++it) {
-            if (ld_acquire(p.bar) >= target) break;
-            if ((it & 15u) == 15u) {
-                if (*reinterpret_cast<volatile unsigned*>(p.bar + 1)) {
-                    ok = 0;
-                    break;
-                }
-                if (gtimer() - t0 > p.spin_ns) {
-                    sf_fail(p, 5);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        fence_proxy_async_global();
-        sb->ok = ok;
-        if (blockIdx.x == 0 && p.trace) {
-            p.trace[2 * epoch + 1] = gtimer();
-            p.trace[SF_TRACE_CLK + epoch] = clock64();
-        }
-    }
-    __syncthreads();
-    return sb->ok != 0;
 }
 
 // ---- tile phases -----------------------------------------------------------
@@ -244,11 +218,69 @@ struct SfState {
     uint32_t a_uses;      // (thread 0)
     uint32_t mma_uses;    // (all threads)
     int w_pending[2];     // a prefetched W load is in flight in this buffer (thread 0)
+    int a_pending;        // the first unit's A load was issued at the barrier (thread 0)
 };
+
+// thread 0: activation tile of unit `un` into the A buffer
+__device__ __forceinline__ void issue_a(const SfParams& P, SfBars* sb, unsigned char* abuf,
+                                        const Unit& un) {
+    tc::mbar_expect_tx(&sb->a_full, (uint32_t)un.nkb * SF_A_BLK);
+    for (int kb = 0; kb < un.nkb; ++kb)
+        tc::tma_load_2d(abuf + kb * SF_A_BLK, &P.amap[un.amap], &sb->a_full, un.k0 + kb * 128,
+                        un.mt * 128);
+}
+
+// next_tp >= 0: right after the wait, thread 0 issues the A-operand loads of
+// this CTA's first unit of tile phase next_tp (its weights are prefetched
+// already), so they overlap the start of the phase.
+__device__ SF_NI bool grid_sync(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem,
+                          unsigned epoch, int next_tp, SfState& st) {
+    __syncthreads();
+    if (threadIdx.x == 0 && blockIdx.x == 0 && p.trace) p.trace[2 * epoch] = gtimer();
+    if (threadIdx.x == 0) {
+        // release: the CTA's writes (ordered before this thread by the
+        // __syncthreads above) become visible with the arrival; the proxy
+        // fences order them with the TMA reads of the next tile phase
+        fence_proxy_async_global();
+        if (p.trace) p.trace[SF_TRACE_ARR + epoch * gridDim.x + blockIdx.x] = gtimer();
+        if (!(p.withhold_arrival && epoch == 1 && blockIdx.x == 0))
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.bar) : "memory");
+        const unsigned target = epoch * gridDim.x;
+        int ok = 1;
+        const unsigned long long t0 = gtimer();
+        for (uint32_t it = 0;; ++it) {
+            if (ld_acquire(p.bar) >= target) break;
+            if ((it & 15u) == 15u) {
+                if (*reinterpret_cast<volatile unsigned*>(p.bar + 1)) {
+                    ok = 0;
+                    break;
+                }
+                if (gtimer() - t0 > p.spin_ns) {
+                    sf_fail(p, 5);
+                    ok = 0;
+                    break;
+                }
+            }
+        }
+        fence_proxy_async_global();
+        sb->ok = ok;
+        Unit un;
+        if (SF_PREISSUE && ok && next_tp >= 0 && unit_at(p, next_tp, blockIdx.x, un)) {
+            issue_a(P, sb, smem, un);
+            st.a_pending = 1;
+        }
+        if (blockIdx.x == 0 && p.trace) {
+            p.trace[2 * epoch + 1] = gtimer();
+            p.trace[SF_TRACE_CLK + epoch] = clock64();
+        }
+    }
+    __syncthreads();
+    return sb->ok != 0;
+}
 
 // Runs this CTA's units of tile phase tp (layer l).  The first unit's weights
 // were prefetched into buffer (tp & 1) at the end of the previous tile phase.
-__device__ bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
+__device__ SF_NI bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
                            int tp, SfState& st) {
     const int l = tp >> 2;
     const int wb = tp & 1;
@@ -262,10 +294,8 @@ __device__ bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsign
         if (threadIdx.x == 0) {
             if (!(first && st.w_pending[wb])) issue_w(P, p, sb, wbuf, wb, l, un);
             st.w_pending[wb] = 0;
-            tc::mbar_expect_tx(&sb->a_full, (uint32_t)un.nkb * SF_A_BLK);
-            for (int kb = 0; kb < un.nkb; ++kb)
-                tc::tma_load_2d(abuf + kb * SF_A_BLK, &P.amap[un.amap], &sb->a_full,
-                                un.k0 + kb * 128, un.mt * 128);
+            if (!(first && st.a_pending)) issue_a(P, sb, abuf, un);
+            st.a_pending = 0;
             const bool tr = p.trace && blockIdx.x == 0 && first;
             if (tr) p.trace[SF_TRACE_TILE + 4 * tp] = clock64();
             bool ok = tc::mbar_wait(&sb->w_full[wb], st.w_uses[wb] & 1u);
@@ -354,21 +384,13 @@ constexpr int SF_GT = 128;  // threads per row group
 struct Grp {
     int id, t, w, lane;  // group in CTA, thread / warp / lane in group
     float* xs;           // row staging [C]
-    float* red;          // reduction scratch [8]
+    float* red;          // reduction scratch [SF_RED]
 };
 
 __device__ __forceinline__ void gsync(const Grp& g) {
     asm volatile("bar.sync %0, %1;" ::"r"(1 + g.id), "r"(SF_GT) : "memory");
 }
 
-__device__ __forceinline__ float group_max(const Grp& g, float v) {
-    v = warp_max(v);
-    if (g.lane == 0) g.red[g.w] = v;
-    gsync(g);
-    const float m = fmaxf(fmaxf(g.red[0], g.red[1]), fmaxf(g.red[2], g.red[3]));
-    gsync(g);
-    return m;
-}
 
 // mean and 1/std of the row in g.xs, bit-identical to ln_warp<EPL>
 template <int EPL>
@@ -398,87 +420,161 @@ __device__ __forceinline__ void group_ln_stats(const Grp& g, int C, float& mean,
 
 __device__ __forceinline__ float f16r(float v) { return __half2float(__float2half_rn(v)); }
 
+// Largest row amax of NQ value sets of this thread, over the group, in one
+// exchange (max is exact, so merging the reductions keeps the bits).
+template <int NQ>
+__device__ __forceinline__ void group_max_n(const Grp& g, float (&m)[NQ]) {
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) {
+        m[j] = warp_max(m[j]);
+        if (g.lane == 0) g.red[8 + 4 * j + g.w] = m[j];
+    }
+    gsync(g);
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) {
+        const float* r = g.red + 8 + 4 * j;
+        m[j] = fmaxf(fmaxf(r[0], r[1]), fmaxf(r[2], r[3]));
+    }
+    gsync(g);
+}
+
 // quantise NV values of this thread (fp16-rounded) with the group's row
 // amax; element i goes to q[t + 128 i]
 template <int NV>
 __device__ __forceinline__ void group_quant_store(const Grp& g, const float (&a)[NV], int8_t* q,
                                                   float* qs) {
-    float m = 0.0f;
+    float m[1] = {0.0f};
 #pragma unroll
-    for (int i = 0; i < NV; ++i) m = fmaxf(m, fabsf(a[i]));
-    const float amax = group_max(g, m);
-    const float inv = q_inv(amax);
+    for (int i = 0; i < NV; ++i) m[0] = fmaxf(m[0], fabsf(a[i]));
+    group_max_n<1>(g, m);
+    const float inv = q_inv(m[0]);
 #pragma unroll
     for (int i = 0; i < NV; ++i) q[g.t + SF_GT * i] = (int8_t)q8(a[i], inv);
-    if (g.t == 0) *qs = q_factor(amax);
+    if (g.t == 0) *qs = q_factor(m[0]);
 }
 
-// exact sum over K slices of the int32 partials of row b, columns t + 128 i
-template <int NV>
-__device__ __forceinline__ void load_part_g(const Grp& g, const int32_t* part, int ks, int B,
-                                            int N, int b, int (&acc)[NV]) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) acc[i] = 0;
-    for (int s = 0; s < ks; ++s) {
-        const int32_t* rp = part + ((int64_t)s * B + b) * N + g.t;
-#pragma unroll
-        for (int i = 0; i < NV; ++i) acc[i] += rp[SF_GT * i];
-    }
+// Trace marks of row phase rp (CTA 0, group 0, row 0): SM clock at entry,
+// when the phase's loaded data has been consumed, after its row reduction,
+// and at its end (slots SF_TRACE_ROW + 4 rp + k).
+constexpr int SF_TRACE_ROW = 1024;
+__device__ __forceinline__ void rmark(const SfHot& p, const Grp& g, int b, int rp, int k) {
+    if (p.trace && b == 0 && g.t == 0 && blockIdx.x == 0) p.trace[SF_TRACE_ROW + 4 * rp + k] = clock64();
 }
+
+// The int32 K-slice partial sums of row b of one GEMM, columns t + 128 i.
+// issue() puts the loads of the first MAXKS slices in flight at once (all
+// loads of a row phase go out before its first use); sum() adds them and
+// any further slices (exact integers: the order does not matter).
+template <int NV, int MAXKS>
+struct PartLd {
+    int v[MAXKS][NV];
+    __device__ __forceinline__ void issue(const Grp& g, const int32_t* part, int ks, int B, int N,
+                                          int b) {
+#pragma unroll
+        for (int s = 0; s < MAXKS; ++s) {
+            const int32_t* rp = part + ((int64_t)s * B + b) * N + g.t;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[s][i] = s < ks ? __ldcg(rp + SF_GT * i) : 0;
+        }
+    }
+    __device__ __forceinline__ void sum(const Grp& g, const int32_t* part, int ks, int B, int N,
+                                        int b, int (&acc)[NV]) const {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            acc[i] = v[0][i];
+#pragma unroll
+            for (int s = 1; s < MAXKS; ++s) acc[i] += v[s][i];
+        }
+        for (int s = MAXKS; s < ks; ++s) {
+            const int32_t* rp = part + ((int64_t)s * B + b) * N + g.t;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) acc[i] += __ldcg(rp + SF_GT * i);
+        }
+    }
+};
+
+// Inputs of a LayerNorm + NMIX token-shift mixes of one row that do not
+// depend on the previous phase (parameters, carried state row), loaded at
+// the start of the row phase.
+template <int EPL, int NMIX>
+struct LnMixIn {
+    static constexpr int NE = EPL / 4;
+    float prev[NE], w[NE], bi[NE], mk[NMIX > 0 ? NMIX : 1][NE];
+    __device__ __forceinline__ void load(const Grp& g, const float* lw, const float* lb,
+                                         const float* const (&mix)[3], const float* srow) {
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            const int c = g.t + SF_GT * i;
+            if (NMIX > 0) prev[i] = srow[c];
+            w[i] = __ldg(lw + c);
+            bi[i] = __ldg(lb + c);
+#pragma unroll
+            for (int m = 0; m < NMIX; ++m) mk[m][i] = __ldg(mix[m] + c);
+        }
+    }
+};
 
 // LN of the row (v: this thread's elements, also staged in g.xs), NMIX
-// token-shift mixes against the carried state row srow (read, then
-// overwritten with LN(v)), each quantised; NMIX = 0 quantises LN(v) itself.
-template <int EPL, int NMIX>
+// token-shift mixes against the carried state row srow (overwritten with
+// LN(v)), each quantised; NMIX = 0 quantises LN(v) itself.
+template <int EPL, int NMIX, int M>
 __device__ __forceinline__ void ln_mix_g(const Grp& g, const float (&v)[EPL / 4], int C,
-                                         const float* lw, const float* lb,
-                                         const float* const (&mix)[3], float* srow,
+                                         const LnMixIn<EPL, M>& in, float* srow,
                                          int8_t* const (&q)[3], float* const (&qs)[3]) {
     constexpr int NE = EPL / 4;
-    float prev[NE], w[NE], bi[NE], mk[NMIX > 0 ? NMIX : 1][NE];
-#pragma unroll
-    for (int i = 0; i < NE; ++i) {
-        const int c = g.t + SF_GT * i;
-        if (NMIX > 0) prev[i] = srow[c];
-        w[i] = __ldg(lw + c);
-        bi[i] = __ldg(lb + c);
-#pragma unroll
-        for (int m = 0; m < NMIX; ++m) mk[m][i] = __ldg(mix[m] + c);
-    }
+    constexpr int NQ = NMIX > 0 ? NMIX : 1;
     float mean, rstd;
     group_ln_stats<EPL>(g, C, mean, rstd);
     float cur[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i)
-        cur[i] = f16r(__fmaf_rn(__fmul_rn(__fsub_rn(v[i], mean), rstd), w[i], bi[i]));
-    if constexpr (NMIX == 0) {
-        group_quant_store<NE>(g, cur, q[0], qs[0]);
-    } else {
+        cur[i] = f16r(__fmaf_rn(__fmul_rn(__fsub_rn(v[i], mean), rstd), in.w[i], in.bi[i]));
+    float a[NQ][NE], m[NQ];
 #pragma unroll
-        for (int m = 0; m < NMIX; ++m) {
-            float a[NE];
+    for (int j = 0; j < NQ; ++j) {
+        m[j] = 0.0f;
 #pragma unroll
-            for (int i = 0; i < NE; ++i)
-                a[i] = f16r(__fmaf_rn(cur[i], mk[m][i],
-                                      __fmul_rn(prev[i], __fsub_rn(1.0f, mk[m][i]))));
-            group_quant_store<NE>(g, a, q[m], qs[m]);
+        for (int i = 0; i < NE; ++i) {
+            a[j][i] = NMIX == 0 ? cur[i]
+                                : f16r(__fmaf_rn(cur[i], in.mk[j][i],
+                                                 __fmul_rn(in.prev[i], __fsub_rn(1.0f, in.mk[j][i]))));
+            m[j] = fmaxf(m[j], fabsf(a[j][i]));
         }
+    }
+    group_max_n<NQ>(g, m);
+#pragma unroll
+    for (int j = 0; j < NQ; ++j) {
+        const float inv = q_inv(m[j]);
+#pragma unroll
+        for (int i = 0; i < NE; ++i) q[j][g.t + SF_GT * i] = (int8_t)q8(a[j][i], inv);
+        if (g.t == 0) *qs[j] = q_factor(m[j]);
+    }
+    if constexpr (NMIX > 0) {
 #pragma unroll
         for (int i = 0; i < NE; ++i) srow[g.t + SF_GT * i] = cur[i];
     }
 }
 
-template <int EPL>
-__device__ __forceinline__ void ln1_mix_g(const Grp& g, const SfHot& p, int l, int b,
-                                          const float (&v)[EPL / 4]) {
-    const int C = p.C;
-    const size_t BC = (size_t)p.B * C;
+// the LN1 + time-mix inputs of layer l for row b; returns the att_xx state row
+template <int EPL, int M>
+__device__ __forceinline__ float* ln1_in(const Grp& g, const SfHot& p, int l, int b,
+                                         LnMixIn<EPL, M>& in) {
+    const size_t BC = (size_t)p.B * p.C;
     const SfLayer& ly = p.layer[l];
     const float* const mix[3] = {ly.mix_k, ly.mix_v, ly.mix_r};
+    float* srow = p.state + (size_t)l * 5 * BC + (size_t)b * p.C;
+    in.load(g, ly.ln1_w, ly.ln1_b, mix, srow);
+    return srow;
+}
+
+template <int EPL>
+__device__ __forceinline__ void ln1_mix_g(const Grp& g, const SfHot& p, int b,
+                                          const float (&v)[EPL / 4], const LnMixIn<EPL, 3>& in,
+                                          float* srow) {
+    const int C = p.C;
     int8_t* const q[3] = {p.q_kx + (size_t)b * C, p.q_vx + (size_t)b * C, p.q_rx + (size_t)b * C};
     float* const qs[3] = {p.s_kx + b, p.s_vx + b, p.s_rx + b};
-    ln_mix_g<EPL, 3>(g, v, C, ly.ln1_w, ly.ln1_b, mix, p.state + (size_t)l * 5 * BC + (size_t)b * C,
-                     q, qs);
+    ln_mix_g<EPL, 3>(g, v, C, in, srow, q, qs);
 }
 
 // embedding + LN1 of layer 0
@@ -486,6 +582,8 @@ template <int EPL>
 __device__ void row_embed(const Grp& g, const SfHot& p, int b) {
     constexpr int NE = EPL / 4;
     const int C = p.C;
+    LnMixIn<EPL, 3> in;
+    float* srow = ln1_in<EPL>(g, p, 0, b, in);
     int t = p.tokens[b];
     t = t < 0 ? 0 : (t >= p.V ? p.V - 1 : t);
     uint16_t e16[NE];
@@ -496,146 +594,238 @@ __device__ void row_embed(const Grp& g, const SfHot& p, int b) {
         v[i] = h2f(e16[i]);
         g.xs[g.t + SF_GT * i] = v[i];
     }
-    ln1_mix_g<EPL>(g, p, 0, b, v);
+    ln1_mix_g<EPL>(g, p, b, v, in, srow);
 #pragma unroll
     for (int i = 0; i < NE; ++i) p.x[(size_t)b * C + g.t + SF_GT * i] = e16[i];
 }
 
+// Slices of the partial sums loaded in one go, per GEMM group (more slices
+// are summed by a second pass): k/v/r, o, ffn key/receptance, ffn value.
+// The 2048-wide rows (EPL 64) hold too many values per thread for that.
+template <int EPL> struct SfKs {
+    static constexpr int KVR = EPL >= 64 ? 1 : 3, O = EPL >= 64 ? 1 : 6;
+    static constexpr int FKR = EPL >= 64 ? 1 : 2, FV = EPL >= 64 ? 1 : 6;
+};
+
+// Each row phase reads (1) inputs that no phase of this step writes before it
+// (carried state, parameters, rows written two or more barriers earlier) and
+// (2) the partial sums of the tile phase just before it.  The *In structs
+// hold (1); the main loop loads them for a group's first row before the
+// barrier that opens the phase, so their latency overlaps the barrier wait.
+
+template <int EPL>
+struct WkvIn {
+    static constexpr int NE = EPL / 4;
+    float aa[NE], bb[NE], pp[NE], u[NE], dec[NE], wk[NE], wv[NE], wr[NE];
+    __device__ __forceinline__ void load(const Grp& g, const SfHot& p, int l, int b) {
+        const size_t BC = (size_t)p.B * p.C;
+        const SfLayer& ly = p.layer[l];
+        const float* s = p.state + (size_t)l * 5 * BC + (size_t)b * p.C + g.t;
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            const int c = g.t + SF_GT * i;
+            aa[i] = s[BC + SF_GT * i];
+            bb[i] = s[2 * BC + SF_GT * i];
+            pp[i] = s[3 * BC + SF_GT * i];
+            u[i] = __ldg(ly.first + c);
+            dec[i] = __ldg(ly.decay + c);
+            wk[i] = h2f(__ldg(ly.wscale[G_K] + c));
+            wv[i] = h2f(__ldg(ly.wscale[G_V] + c));
+            wr[i] = h2f(__ldg(ly.wscale[G_R] + c));
+        }
+    }
+};
+
 // k, v, r -> WKV -> r*y, quantised
 template <int EPL>
-__device__ void row_wkv(const Grp& g, const SfHot& p, int l, int b) {
+__device__ void row_wkv(const Grp& g, const SfHot& p, int l, int b, WkvIn<EPL>& in) {
+    rmark(p, g, b, 1 + 4 * l, 0);
     constexpr int NE = EPL / 4;
     const int C = p.C;
     const size_t BC = (size_t)p.B * C;
-    const SfLayer& ly = p.layer[l];
     float* s = p.state + (size_t)l * 5 * BC + (size_t)b * C + g.t;
+    const float sk = __ldcg(p.s_kx + b), sv = __ldcg(p.s_vx + b), sr = __ldcg(p.s_rx + b);
+    PartLd<NE, SfKs<EPL>::KVR> lk, lv, lr;
+    const int ks = p.ks[G_K];
+    lk.issue(g, p.part[G_K], ks, p.B, C, b);
+    lv.issue(g, p.part[G_V], ks, p.B, C, b);
+    lr.issue(g, p.part[G_R], ks, p.B, C, b);
     int ak[NE], av[NE], ar[NE];
-    load_part_g<NE>(g, p.part[G_K], p.ks[G_K], p.B, C, b, ak);
-    load_part_g<NE>(g, p.part[G_V], p.ks[G_V], p.B, C, b, av);
-    load_part_g<NE>(g, p.part[G_R], p.ks[G_R], p.B, C, b, ar);
-    float aa[NE], bb[NE], pp[NE], u[NE], dec[NE], wk[NE], wv[NE], wr[NE];
-#pragma unroll
-    for (int i = 0; i < NE; ++i) {
-        const int c = g.t + SF_GT * i;
-        aa[i] = s[BC + SF_GT * i];
-        bb[i] = s[2 * BC + SF_GT * i];
-        pp[i] = s[3 * BC + SF_GT * i];
-        u[i] = __ldg(ly.first + c);
-        dec[i] = __ldg(ly.decay + c);
-        wk[i] = h2f(__ldg(ly.wscale[G_K] + c));
-        wv[i] = h2f(__ldg(ly.wscale[G_V] + c));
-        wr[i] = h2f(__ldg(ly.wscale[G_R] + c));
-    }
-    const float sk = p.s_kx[b], sv = p.s_vx[b], sr = p.s_rx[b];
+    lk.sum(g, p.part[G_K], ks, p.B, C, b, ak);
+    lv.sum(g, p.part[G_V], ks, p.B, C, b, av);
+    lr.sum(g, p.part[G_R], ks, p.B, C, b, ar);
     float ry[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
-        const float k = epi_dequant(ak[i], sk, wk[i]);
-        const float v = epi_dequant(av[i], sv, wv[i]);
-        const float r = f16r(epi_sigmoid(epi_dequant(ar[i], sr, wr[i])));
+        const float k = epi_dequant(ak[i], sk, in.wk[i]);
+        const float v = epi_dequant(av[i], sv, in.wv[i]);
+        const float r = f16r(epi_sigmoid(epi_dequant(ar[i], sr, in.wr[i])));
         const float y = p.conv == KB_WKV_STEP_REF
-                            ? wkv_step<KB_WKV_STEP_REF>(aa[i], bb[i], pp[i], k, v, u[i], dec[i])
-                            : wkv_step<KB_WKV_PRODUCTION>(aa[i], bb[i], pp[i], k, v, u[i], dec[i]);
+                            ? wkv_step<KB_WKV_STEP_REF>(in.aa[i], in.bb[i], in.pp[i], k, v, in.u[i], in.dec[i])
+                            : wkv_step<KB_WKV_PRODUCTION>(in.aa[i], in.bb[i], in.pp[i], k, v, in.u[i], in.dec[i]);
         ry[i] = f16r(__fmul_rn(r, y));
     }
+    rmark(p, g, b, 1 + 4 * l, 1);
     group_quant_store<NE>(g, ry, p.q_ry + (size_t)b * C, p.s_ry + b);
+    rmark(p, g, b, 1 + 4 * l, 2);
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
-        s[BC + SF_GT * i] = aa[i];
-        s[2 * BC + SF_GT * i] = bb[i];
-        s[3 * BC + SF_GT * i] = pp[i];
+        s[BC + SF_GT * i] = in.aa[i];
+        s[2 * BC + SF_GT * i] = in.bb[i];
+        s[3 * BC + SF_GT * i] = in.pp[i];
     }
+    rmark(p, g, b, 1 + 4 * l, 3);
 }
+
+template <int EPL>
+struct AttIn {
+    static constexpr int NE = EPL / 4;
+    LnMixIn<EPL, 2> ln;
+    float* srow;
+    float x[NE], wo[NE];
+    __device__ __forceinline__ void load(const Grp& g, const SfHot& p, int l, int b) {
+        const size_t BC = (size_t)p.B * p.C;
+        const SfLayer& ly = p.layer[l];
+        const float* const mix[3] = {ly.fmix_k, ly.fmix_r, nullptr};
+        srow = p.state + (size_t)l * 5 * BC + 4 * BC + (size_t)b * p.C;
+        ln.load(g, ly.ln2_w, ly.ln2_b, mix, srow);
+        const uint16_t* xr = p.x + (size_t)b * p.C + g.t;
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            x[i] = h2f(xr[SF_GT * i]);
+            wo[i] = h2f(__ldg(ly.wscale[G_O] + g.t + SF_GT * i));
+        }
+    }
+};
 
 // x += (r*y) @ Ow; LN2 + the two channel-mix outputs, quantised; ffn_xx <- LN2(x)
 template <int EPL>
-__device__ void row_att_out(const Grp& g, const SfHot& p, int l, int b) {
+__device__ void row_att_out(const Grp& g, const SfHot& p, int l, int b, AttIn<EPL>& in) {
+    rmark(p, g, b, 2 + 4 * l, 0);
     constexpr int NE = EPL / 4;
     const int C = p.C;
-    const size_t BC = (size_t)p.B * C;
-    const SfLayer& ly = p.layer[l];
-    int acc[NE];
-    load_part_g<NE>(g, p.part[G_O], p.ks[G_O], p.B, C, b, acc);
     uint16_t* xr = p.x + (size_t)b * C + g.t;
-    float v[NE], wo[NE];
+    const float sa = __ldcg(p.s_ry + b);
+    PartLd<NE, SfKs<EPL>::O> lo;
+    lo.issue(g, p.part[G_O], p.ks[G_O], p.B, C, b);
+    int acc[NE];
+    lo.sum(g, p.part[G_O], p.ks[G_O], p.B, C, b, acc);
+    float v[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
-        v[i] = h2f(xr[SF_GT * i]);
-        wo[i] = h2f(__ldg(ly.wscale[G_O] + g.t + SF_GT * i));
-    }
-    const float sa = p.s_ry[b];
-#pragma unroll
-    for (int i = 0; i < NE; ++i) {
-        v[i] = f16r(epi_gate_resid(1.0f, epi_dequant(acc[i], sa, wo[i]), v[i]));
+        v[i] = f16r(epi_gate_resid(1.0f, epi_dequant(acc[i], sa, in.wo[i]), in.x[i]));
         g.xs[g.t + SF_GT * i] = v[i];
     }
-    const float* const mix[3] = {ly.fmix_k, ly.fmix_r, nullptr};
+    rmark(p, g, b, 2 + 4 * l, 1);
     int8_t* const q[3] = {p.q_kx + (size_t)b * C, p.q_rx + (size_t)b * C, nullptr};
     float* const qs[3] = {p.s_kx + b, p.s_rx + b, nullptr};
-    ln_mix_g<EPL, 2>(g, v, C, ly.ln2_w, ly.ln2_b, mix,
-                     p.state + (size_t)l * 5 * BC + 4 * BC + (size_t)b * C, q, qs);
+    ln_mix_g<EPL, 2>(g, v, C, in.ln, in.srow, q, qs);
+    rmark(p, g, b, 2 + 4 * l, 2);
 #pragma unroll
     for (int i = 0; i < NE; ++i) xr[SF_GT * i] = f2h(v[i]);
+    rmark(p, g, b, 2 + 4 * l, 3);
 }
+
+// the ffn-mid phase has no early inputs worth holding in registers (its
+// per-channel scales are loaded beside the partial sums)
+template <int EPL>
+struct MidIn {
+    __device__ __forceinline__ void load(const Grp&, const SfHot&, int, int) {}
+};
 
 // kk = relu(k)^2 quantised per row (F = 4C: EPL values per thread);
 // r2 = sigmoid(r) (fp16)
 template <int EPL>
-__device__ void row_ffn_mid(const Grp& g, const SfHot& p, int l, int b) {
+__device__ void row_ffn_mid(const Grp& g, const SfHot& p, int l, int b, MidIn<EPL>&) {
+    rmark(p, g, b, 3 + 4 * l, 0);
     constexpr int NE = EPL / 4, NF = EPL;
     const int C = p.C, F = p.F;
     const SfLayer& ly = p.layer[l];
-    int ak[NF], ar[NE];
-    load_part_g<NF>(g, p.part[G_FK], p.ks[G_FK], p.B, F, b, ak);
-    load_part_g<NE>(g, p.part[G_FR], p.ks[G_FR], p.B, C, b, ar);
     float wk[NF], wr[NE];
 #pragma unroll
     for (int i = 0; i < NF; ++i) wk[i] = h2f(__ldg(ly.wscale[G_FK] + g.t + SF_GT * i));
 #pragma unroll
     for (int i = 0; i < NE; ++i) wr[i] = h2f(__ldg(ly.wscale[G_FR] + g.t + SF_GT * i));
-    const float sk = p.s_kx[b], sr = p.s_rx[b];
+    const float sk = __ldcg(p.s_kx + b), sr = __ldcg(p.s_rx + b);
+    const int ks = p.ks[G_FK];
+    PartLd<NF, SfKs<EPL>::FKR> lk;
+    PartLd<NE, SfKs<EPL>::FKR> lr;
+    lk.issue(g, p.part[G_FK], ks, p.B, F, b);
+    lr.issue(g, p.part[G_FR], ks, p.B, C, b);
+    int ak[NF], ar[NE];
+    lk.sum(g, p.part[G_FK], ks, p.B, F, b, ak);
+    lr.sum(g, p.part[G_FR], ks, p.B, C, b, ar);
     float kk[NF];
 #pragma unroll
     for (int i = 0; i < NF; ++i) kk[i] = f16r(epi_relu_sq(epi_dequant(ak[i], sk, wk[i])));
+    rmark(p, g, b, 3 + 4 * l, 1);
     group_quant_store<NF>(g, kk, p.q_kk + (size_t)b * F, p.s_kk + b);
+    rmark(p, g, b, 3 + 4 * l, 2);
 #pragma unroll
     for (int i = 0; i < NE; ++i)
         p.r2[(size_t)b * C + g.t + SF_GT * i] = f2h(epi_sigmoid(epi_dequant(ar[i], sr, wr[i])));
+    rmark(p, g, b, 3 + 4 * l, 3);
 }
+
+template <int EPL>
+struct OutIn {
+    static constexpr int NE = EPL / 4;
+    LnMixIn<EPL, 3> ln;  // LN1 of layer l+1, or ln_out (mixes unused)
+    float* srow;
+    float x[NE], gt[NE], wv[NE];
+    __device__ __forceinline__ void load(const Grp& g, const SfHot& p, int l, int b) {
+        const SfLayer& ly = p.layer[l];
+        if (l + 1 < p.L) {
+            srow = ln1_in<EPL>(g, p, l + 1, b, ln);
+        } else {
+            srow = nullptr;
+#pragma unroll
+            for (int i = 0; i < NE; ++i) {
+                ln.w[i] = __ldg(p.ln_out_w + g.t + SF_GT * i);
+                ln.bi[i] = __ldg(p.ln_out_b + g.t + SF_GT * i);
+            }
+        }
+        const uint16_t* xr = p.x + (size_t)b * p.C + g.t;
+        const uint16_t* r2 = p.r2 + (size_t)b * p.C + g.t;
+#pragma unroll
+        for (int i = 0; i < NE; ++i) {
+            x[i] = h2f(xr[SF_GT * i]);
+            gt[i] = h2f(r2[SF_GT * i]);
+            wv[i] = h2f(__ldg(ly.wscale[G_FV] + g.t + SF_GT * i));
+        }
+    }
+};
 
 // x += r2 * (kk @ Vw); then LN1 + mix of layer l+1, or ln_out + quantisation
 template <int EPL>
-__device__ void row_ffn_out(const Grp& g, const SfHot& p, int l, int b) {
+__device__ void row_ffn_out(const Grp& g, const SfHot& p, int l, int b, OutIn<EPL>& in) {
+    rmark(p, g, b, 4 + 4 * l, 0);
     constexpr int NE = EPL / 4;
     const int C = p.C;
-    const SfLayer& ly = p.layer[l];
-    int acc[NE];
-    load_part_g<NE>(g, p.part[G_FV], p.ks[G_FV], p.B, C, b, acc);
     uint16_t* xr = p.x + (size_t)b * C + g.t;
-    const uint16_t* r2 = p.r2 + (size_t)b * C + g.t;
-    float v[NE], gt[NE], wv[NE];
+    const float sa = __ldcg(p.s_kk + b);
+    PartLd<NE, SfKs<EPL>::FV> lf;
+    lf.issue(g, p.part[G_FV], p.ks[G_FV], p.B, C, b);
+    int acc[NE];
+    lf.sum(g, p.part[G_FV], p.ks[G_FV], p.B, C, b, acc);
+    float v[NE];
 #pragma unroll
     for (int i = 0; i < NE; ++i) {
-        v[i] = h2f(xr[SF_GT * i]);
-        gt[i] = h2f(r2[SF_GT * i]);
-        wv[i] = h2f(__ldg(ly.wscale[G_FV] + g.t + SF_GT * i));
-    }
-    const float sa = p.s_kk[b];
-#pragma unroll
-    for (int i = 0; i < NE; ++i) {
-        v[i] = f16r(epi_gate_resid(gt[i], epi_dequant(acc[i], sa, wv[i]), v[i]));
+        v[i] = f16r(epi_gate_resid(in.gt[i], epi_dequant(acc[i], sa, in.wv[i]), in.x[i]));
         g.xs[g.t + SF_GT * i] = v[i];
     }
+    rmark(p, g, b, 4 + 4 * l, 1);
     if (l + 1 < p.L) {
-        ln1_mix_g<EPL>(g, p, l + 1, b, v);
+        ln1_mix_g<EPL>(g, p, b, v, in.ln, in.srow);
     } else {
-        const float* const mix[3] = {nullptr, nullptr, nullptr};
         int8_t* const q[3] = {p.q_kx + (size_t)b * C, nullptr, nullptr};
         float* const qs[3] = {p.s_kx + b, nullptr, nullptr};
-        ln_mix_g<EPL, 0>(g, v, C, p.ln_out_w, p.ln_out_b, mix, nullptr, q, qs);
+        ln_mix_g<EPL, 0>(g, v, C, in.ln, nullptr, q, qs);
     }
+    rmark(p, g, b, 4 + 4 * l, 2);
 #pragma unroll
     for (int i = 0; i < NE; ++i) xr[SF_GT * i] = f2h(v[i]);
+    rmark(p, g, b, 4 + 4 * l, 3);
 }
 
 template <int EPL>
@@ -666,7 +856,7 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     tc::fence_after_sync();
     const uint32_t tmem = sb->tmem_base;
 
-    SfState st{{0, 0}, 0, 0, {0, 0}};
+    SfState st{{0, 0}, 0, 0, {0, 0}, 0};
     // weights of the first tile phase, fetched while the embedding runs
     if (threadIdx.x == 0) {
         Unit u0;
@@ -681,36 +871,46 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     grp.t = threadIdx.x & (SF_GT - 1);
     grp.w = warp & 3;
     grp.lane = lane;
-    grp.xs = reinterpret_cast<float*>(smem + SF_ROW_OFF) + grp.id * (SF_MAX_C + 8);
+    grp.xs = reinterpret_cast<float*>(smem + SF_ROW_OFF) + grp.id * (SF_MAX_C + SF_RED);
     grp.red = grp.xs + SF_MAX_C;
     const int gw = grp.id * gridDim.x + blockIdx.x, nw = 2 * gridDim.x;
     unsigned epoch = 0;
     bool ok = true;
     for (int b = gw; b < p.B; b += nw) row_embed<EPL>(grp, p, b);
-    ok = grid_sync(p, sb, ++epoch);
+    ok = grid_sync(P, p, sb, smem, ++epoch, 0, st);
+// a row phase: inputs of the group's first row loaded before the barrier
+#define SF_ROWS(IN, FN)                                                  \
+    {                                                                    \
+        IN<EPL> in;                                                      \
+        if (SF_PREROW && gw < p.B) in.load(grp, p, l, gw);               \
+        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, -1, st))) break;   \
+        for (int b = gw; b < p.B; b += nw) {                             \
+            if (!SF_PREROW || b != gw) in.load(grp, p, l, b);            \
+            FN<EPL>(grp, p, l, b, in);                                   \
+        }                                                                \
+    }
     for (int l = 0; l < p.L && ok; ++l) {
         tile_phase(P, p, sb, smem, tmem, 4 * l + 0, st);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        for (int b = gw; b < p.B; b += nw) row_wkv<EPL>(grp, p, l, b);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
+        SF_ROWS(WkvIn, row_wkv)
+        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 1, st))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 1, st);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        for (int b = gw; b < p.B; b += nw) row_att_out<EPL>(grp, p, l, b);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
+        SF_ROWS(AttIn, row_att_out)
+        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 2, st))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 2, st);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        for (int b = gw; b < p.B; b += nw) row_ffn_mid<EPL>(grp, p, l, b);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
+        SF_ROWS(MidIn, row_ffn_mid)
+        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 3, st))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 3, st);
-        if (!(ok = grid_sync(p, sb, ++epoch))) break;
-        for (int b = gw; b < p.B; b += nw) row_ffn_out<EPL>(grp, p, l, b);
-        if (l + 1 < p.L && !(ok = grid_sync(p, sb, ++epoch))) break;
+        SF_ROWS(OutIn, row_ffn_out)
+        if (l + 1 < p.L && !(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * (l + 1), st))) break;
     }
+#undef SF_ROWS
     // a prefetched weight load that no phase consumed (abort) must land
     // before the CTA exits
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i)
             if (st.w_pending[i]) tc::mbar_wait(&sb->w_full[i], st.w_uses[i] & 1u);
+        if (st.a_pending) tc::mbar_wait(&sb->a_full, st.a_uses & 1u);
+    }
     tc::fence_before_sync();
     __syncthreads();
     if (warp == 0) {
@@ -998,11 +1198,13 @@ extern "C" int kb_step_forward(kb_model* m, const int32_t* tokens, int B, float*
     }
 }
 
-// Profiling aid: when trace is non-NULL (device, >= 1024 u64), CTA 0 of
+// Profiling aid: when trace is non-NULL (device, >= 2048 u64), CTA 0 of
 // every later kb_step_forward records %globaltimer at each grid barrier's
 // entry (even slots) and exit (odd slots), and for its first unit of tile
 // phase tp at slots 512 + 4 tp + {loads issued, operands landed, MMAs done,
-// partials stored} and at barrier exits at 768 + epoch, as SM clock counts.
+// partials stored} and at barrier exits at 768 + epoch, as SM clock counts,
+// and for row 0 of row phase rp (1 + 4 layer + {wkv, ln2, ffn mid, ln1})
+// at slots 1024 + 4 rp + {entry, data consumed, row reduction done, end}.
 // NULL turns it off.
 extern "C" int kb_step_set_trace(unsigned long long* trace) {
     kb::g_step_trace = trace;

@@ -28,7 +28,7 @@ def main() -> None:
     shape = (12, 768, 3072, 50277) if a.model == "169m" else (24, 2048, 8192, 50277)
     m = RWKVModel(random_weights(*shape, seed=0), wdtype="i8")
     L, B = shape[0], a.B
-    tr = torch.zeros(1024, dtype=torch.int64, device="cuda")
+    tr = torch.zeros(65536, dtype=torch.int64, device="cuda")
     st, ws = m.new_state(B), m.new_step_workspace(B)
     lg, ss = m.new_logits(B, 1), m.new_stats(B, 1)
     tok = torch.zeros(B, dtype=torch.int32, device="cuda")
@@ -63,6 +63,39 @@ def main() -> None:
           "landed->MMA done MMA->stored")
     for k, nm in enumerate(["kvr", "o", "ffn", "fv"]):
         print(f"  {nm:4s}", np.round(acc[k] / L, 2))
+    print("row phases (k SM cycles, mean over layers): barrier exit->entry entry->data "
+          "data->reduced reduced->end")
+    racc = np.zeros((4, 4))
+    for l in range(L):
+        for j in range(4):
+            rp = 1 + 4 * l + j
+            r0 = t[1024 + 4 * rp:1024 + 4 * rp + 4]
+            ex_clk = t[768 + 8 * l + 2 + 2 * j]
+            racc[j] += np.array([r0[0] - ex_clk, r0[1] - r0[0], r0[2] - r0[1], r0[3] - r0[2]]) / 1e3
+    for k, nm in enumerate(["wkv", "ln2", "mid", "ln1"]):
+        print(f"  {nm:4s}", np.round(racc[k] / L, 2))
+    # every CTA's arrival time per barrier: the phase's critical path is the
+    # last arrival minus the previous barrier's release
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    E = e - 1
+    arr = t[2048:2048 + (E + 1) * G].reshape(E + 1, G)
+    crit = np.zeros(8)
+    med = np.zeros(8)
+    rel = np.zeros(8)
+    slow = np.zeros(G)
+    for ep in range(2, E + 1):
+        k = (ep - 2) % 8
+        crit[k] += (arr[ep].max() - ex[ep - 1]) / 1e3
+        med[k] += (np.median(arr[ep]) - ex[ep - 1]) / 1e3
+        rel[k] += (ex[ep] - arr[ep].max()) / 1e3
+        slow[arr[ep].argmax()] += 1
+    print("per phase (us, summed over layers): critical (last arrival - previous release), "
+          "median arrival, release after last arrival")
+    for k, nm in enumerate(["kvr", "wkv", "o", "ln2", "ffn", "mid", "fv", "ln1"]):
+        print(f"  {nm:4s} crit {crit[k]:7.1f}  median {med[k]:7.1f}  release {rel[k]:6.1f}")
+    print(f"  total crit {crit.sum():.1f}  release {rel.sum():.1f}")
+    top = np.argsort(-slow)[:8]
+    print("slowest CTA counts:", {int(i): int(slow[i]) for i in top})
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.steps):

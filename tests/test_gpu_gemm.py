@@ -120,3 +120,47 @@ def test_cta_pair_tiles_bit_identical(torch, epi, M, N, K, bf16):
     if epi == 0:
         ref = A.float() @ W.float().t()
         assert (got - ref).abs().max().item() <= 1e-4 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "i8"])
+@pytest.mark.parametrize("M,tile", [(1, 0), (300, 0), (300, 64), (9000, 0), (70000, 0),
+                                     (70000, 512)])
+def test_grouped_kvr_equals_three_launches(torch, dtype, M, tile):
+    """kb_gemm_kvr (one launch: k, v fp32, r = sigmoid fp16; the reference's
+    det_matmul_tc_3way_async.cu:50-251) gives the bits of three single
+    launches, on single-CTA and CTA-pair tilings."""
+    from krunch_b200 import _native as N
+    C = 768
+    g = torch.Generator(device="cuda").manual_seed(M + tile)
+    i8 = dtype == "i8"
+    if i8:
+        A = [torch.randint(-127, 128, (M, C), device="cuda", dtype=torch.int8, generator=g)
+             for _ in range(3)]
+        W = [torch.randint(-127, 128, (C, C), device="cuda", dtype=torch.int8, generator=g)
+             for _ in range(3)]
+        sa = [torch.rand(M, device="cuda", generator=g) * 1e-2 for _ in range(3)]
+        sw = [(torch.rand(C, device="cuda", generator=g) * 1e-2).half() for _ in range(3)]
+    else:
+        dt = torch.bfloat16 if dtype == "bf16" else torch.float16
+        A = [(torch.randn((M, C), device="cuda", generator=g) * 0.5).to(dt) for _ in range(3)]
+        W = [(torch.randn((C, C), device="cuda", generator=g) * 0.05).to(dt) for _ in range(3)]
+        sa, sw = [None] * 3, [None] * 3
+    kind = {"f16": N.KB_F16, "bf16": N.KB_BF16, "i8": N.KB_I8}[dtype]
+    k = torch.empty((M, C), device="cuda")
+    v = torch.empty((M, C), device="cuda")
+    r = torch.empty((M, C), device="cuda", dtype=torch.float16)
+    p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    N.call("kb_gemm_kvr", kind, A[0].data_ptr(), A[1].data_ptr(), A[2].data_ptr(), C,
+           p(sa[0]), p(sa[1]), p(sa[2]), W[0].data_ptr(), W[1].data_ptr(), W[2].data_ptr(), C,
+           p(sw[0]), p(sw[1]), p(sw[2]), M, C, C, k.data_ptr(), v.data_ptr(), r.data_ptr(), C,
+           tile, N.stream_ptr())
+    for j, (out, epi) in enumerate(((k, N.KB_EPI_F32), (v, N.KB_EPI_F32), (r, N.KB_EPI_SIGMOID))):
+        ref = torch.empty_like(out)
+        if i8:
+            N.call("kb_gemm_i8", A[j].data_ptr(), C, sa[j].data_ptr(), W[j].data_ptr(), C,
+                   sw[j].data_ptr(), M, C, C, epi, ref.data_ptr(), C, None, None, tile,
+                   N.stream_ptr())
+        else:
+            N.call("kb_gemm_tiled", kind, A[j].data_ptr(), C, W[j].data_ptr(), C, M, C, C, epi,
+                   ref.data_ptr(), C, None, None, tile, N.stream_ptr())
+        assert torch.equal(out, ref), (dtype, M, tile, j)
