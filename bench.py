@@ -22,6 +22,11 @@ on rank 0 with all host threads.
 
 Multi-GPU: one process per GPU (torchrun); each rank compresses its own 64
 chunks (weak scaling, no data-path collective).
+
+box   : BASELINE configs[3] on a bounded slice (--box-chunks 1 MiB log-line
+        chunks per GPU): chunk i on rank i mod G through the engine's batch
+        API with the w8a8 model, then the NCCL length all-gather + payload
+        gather and the rank-0 stitch; reports the collective's share.
 """
 from __future__ import annotations
 
@@ -220,6 +225,67 @@ def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
             "clocks": clk.summary()}
 
 
+def bench_box(args, rank, world, dev, max_over_ranks, barrier):
+    """configs[3] on a bounded slice: seeded log lines cut into 1 MiB
+    UTF-8-safe chunks (reference chunking.py:115-138), chunk i compressed on
+    rank i mod G by the w8a8 model through the engine's public batch API,
+    then the length all-gather + payload gather over NCCL and the rank-0
+    stitch into one .krunch blob (krunch_b200.distributed, the path of
+    `krunch compress` under torchrun).  Timed: host text -> stitched blob,
+    synchronised device and barrier on both sides, max over ranks; the
+    collective is timed on its own as well."""
+    import zlib
+
+    import torch
+    from krunch_b200 import chunking
+    from krunch_b200 import distributed as kd
+    from krunch_b200 import inference
+    from krunch_b200.inference import CodecConfig, decode_header, encode_header
+    from krunch_b200.synth import log_lines
+    from krunch_b200.tokenizer import ByteTokenizer
+    cb = args.box_chunk_bytes
+    raw = log_lines(args.box_chunks * world * cb, seed=4)
+    eng = inference.engine
+    eng.load(CodecConfig(family="169m", cdf_bits=args.cdf_bits, wdtype="i8"), ByteTokenizer(), dev)
+    eng.compress_chunks_batched([raw[:4096]] * 2)  # warm-up: model, plans, graphs
+    chunks = chunking.split(raw, chunk_size=cb)
+    mine = [chunks[i] for i in kd.shard(len(chunks), rank, world)]
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    local = eng.compress_chunks_batched(mine)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    payloads = kd.gather_payloads(local, len(chunks))
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    blob = None
+    if payloads is not None:
+        crc = zlib.crc32(raw) & 0xFFFFFFFF
+        blob = encode_header(len(raw), len(chunks), crc) + b"".join(
+            chunking.pack_entries(chunks, payloads))
+    t3 = time.perf_counter()
+    barrier()
+    total_s = max_over_ranks(t3 - t0)
+    gather_s = max_over_ranks(t2 - t1)
+    compress_s = max_over_ranks(t1 - t0)
+    ok = None
+    if blob is not None:
+        hdr = decode_header(blob)
+        ents = chunking.parse_entries(blob[inference.HEADER_SIZE:], hdr["n_chunks"])
+        ok = (hdr["original_len"] == len(raw) and hdr["flags"] == 0 and
+              [ol for ol, _ in ents] == [len(c) for c in chunks])
+    return {"workload": f"configs[3] slice: {len(chunks)} log-line chunks of {cb >> 10} KiB "
+                        f"({args.box_chunks} per GPU), w8a8 RWKV-4-169M, round-robin over "
+                        f"{world} GPU(s), NCCL length all-gather + payload gather, rank-0 stitch",
+            "value": len(raw) / total_s / 1e6, "unit": "MB/s", "input_bytes": len(raw),
+            "blob_bytes": None if blob is None else len(blob),
+            "bits_per_byte": None if blob is None else 8.0 * len(blob) / len(raw),
+            "s_total": total_s, "s_compress": compress_s, "s_gather": gather_s,
+            "collective_share": gather_s / total_s, "blob_ok": ok,
+            "timing": "host perf_counter around device-synchronised steps, max over ranks"}
+
+
 def config(args):
     name = "RWKV-4-169M" if args.model == "169m" else "RWKV-4 1.5B architecture"
     wl = ("configs[1] compress, packed forward, 1 GPU per rank" if args.model == "169m"
@@ -253,6 +319,10 @@ def main():
                     help="skip the configs[2] decompress line (w8a8, B=256 x 2048 steps)")
     ap.add_argument("--dec-B", type=int, default=256)
     ap.add_argument("--dec-T", type=int, default=2048)
+    ap.add_argument("--no-box", action="store_true",
+                    help="skip the configs[3] slice (log lines, 1 MiB chunks, NCCL stitch)")
+    ap.add_argument("--box-chunks", type=int, default=8, help="1 MiB chunks per GPU")
+    ap.add_argument("--box-chunk-bytes", type=int, default=1 << 20)
     args = ap.parse_args()
     global SHAPE
     SHAPE = SHAPES[args.model]
@@ -384,6 +454,9 @@ def main():
     extra = {}
     if not args.no_decompress:
         extra["decompress"] = bench_decompress(args, rank, world, stream, max_over_ranks, barrier)
+
+    if not args.no_box:
+        extra["box"] = bench_box(args, rank, world, dev, max_over_ranks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

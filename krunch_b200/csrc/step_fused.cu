@@ -43,15 +43,6 @@
 
 namespace kb {
 
-#ifndef SF_PREISSUE
-#define SF_PREISSUE 0
-#endif
-#ifndef SF_PREROW
-#define SF_PREROW 0
-#endif
-#ifndef SF_NI
-#define SF_NI
-#endif
 
 constexpr int SF_NT = 256;                       // 8 warps
 constexpr int SF_BN = 64;                        // N columns per unit
@@ -66,6 +57,7 @@ constexpr size_t SF_ROW_OFF = SF_A_BYTES + 2 * SF_W_BYTES + 256;
 constexpr uint32_t SF_IDESC = tc::idesc_i8(128, SF_BN);
 constexpr int SF_TRACE_TILE = 512;  // + 4 tp: SM clock of CTA 0's first unit
 constexpr int SF_TRACE_CLK = 768;   // + epoch: SM clock at barrier exit
+constexpr int SF_TRACE_TILE2 = 1536;  // + 4 tp: tile phase entry, unit found, W issued
 constexpr int SF_TRACE_ARR = 2048;  // + epoch * grid + cta: %globaltimer at each CTA's arrival
 constexpr unsigned long long SF_SPIN_NS = 2000000000ull;  // grid-barrier wait bound: 2 s
 
@@ -114,11 +106,20 @@ static_assert(SF_SMEM <= 232448, "shared memory per block");
 
 __device__ int g_step_error = 0;
 
+struct Unit {
+    int g, amap, N, mt, nt, k0, nkb, ks;
+};
+
 struct SfBars {
     uint64_t a_full, w_full[2], mma_done;
     uint32_t tmem_base;
     int ok;
+    // this CTA's first unit of each tile-phase kind (kvr, o, ffn, fv): the
+    // same for every layer, found once at kernel start
+    Unit first[4];
+    int has_first[4];
 };
+static_assert(sizeof(SfBars) <= 256, "SfBars fits its shared-memory slot");
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
     unsigned v;
@@ -172,10 +173,6 @@ __device__ __forceinline__ int phase_jobs(const SfHot& p, int tp, Job (&j)[3]) {
     }
 }
 
-struct Unit {
-    int g, amap, N, mt, nt, k0, nkb, ks;
-};
-
 __device__ __forceinline__ int units_of(const SfHot& p, const Job& jb) {
     return ((p.B + 127) / 128) * (jb.N / SF_BN) * jb.ks;
 }
@@ -218,7 +215,6 @@ struct SfState {
     uint32_t a_uses;      // (thread 0)
     uint32_t mma_uses;    // (all threads)
     int w_pending[2];     // a prefetched W load is in flight in this buffer (thread 0)
-    int a_pending;        // the first unit's A load was issued at the barrier (thread 0)
 };
 
 // thread 0: activation tile of unit `un` into the A buffer
@@ -230,11 +226,7 @@ __device__ __forceinline__ void issue_a(const SfParams& P, SfBars* sb, unsigned 
                         un.mt * 128);
 }
 
-// next_tp >= 0: right after the wait, thread 0 issues the A-operand loads of
-// this CTA's first unit of tile phase next_tp (its weights are prefetched
-// already), so they overlap the start of the phase.
-__device__ SF_NI bool grid_sync(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem,
-                          unsigned epoch, int next_tp, SfState& st) {
+__device__ bool grid_sync(const SfHot& p, SfBars* sb, unsigned epoch) {
     __syncthreads();
     if (threadIdx.x == 0 && blockIdx.x == 0 && p.trace) p.trace[2 * epoch] = gtimer();
     if (threadIdx.x == 0) {
@@ -264,11 +256,6 @@ __device__ SF_NI bool grid_sync(const SfParams& P, const SfHot& p, SfBars* sb, u
         }
         fence_proxy_async_global();
         sb->ok = ok;
-        Unit un;
-        if (SF_PREISSUE && ok && next_tp >= 0 && unit_at(p, next_tp, blockIdx.x, un)) {
-            issue_a(P, sb, smem, un);
-            st.a_pending = 1;
-        }
         if (blockIdx.x == 0 && p.trace) {
             p.trace[2 * epoch + 1] = gtimer();
             p.trace[SF_TRACE_CLK + epoch] = clock64();
@@ -280,7 +267,7 @@ __device__ SF_NI bool grid_sync(const SfParams& P, const SfHot& p, SfBars* sb, u
 
 // Runs this CTA's units of tile phase tp (layer l).  The first unit's weights
 // were prefetched into buffer (tp & 1) at the end of the previous tile phase.
-__device__ SF_NI bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
+__device__ bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, unsigned char* smem, uint32_t tmem,
                            int tp, SfState& st) {
     const int l = tp >> 2;
     const int wb = tp & 1;
@@ -288,14 +275,21 @@ __device__ SF_NI bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, 
     unsigned char* wbuf = smem + SF_A_BYTES + wb * SF_W_BYTES;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     bool first = true;
+    if (p.trace && blockIdx.x == 0 && threadIdx.x == 0) p.trace[SF_TRACE_TILE2 + 4 * tp] = clock64();
     for (int u = blockIdx.x;; u += gridDim.x) {
         Unit un;
-        if (!unit_at(p, tp, u, un)) break;
+        if (first) {
+            if (!sb->has_first[tp & 3]) break;
+            un = sb->first[tp & 3];
+        } else if (!unit_at(p, tp, u, un)) {
+            break;
+        }
         if (threadIdx.x == 0) {
+            if (p.trace && blockIdx.x == 0 && first) p.trace[SF_TRACE_TILE2 + 4 * tp + 1] = clock64();
             if (!(first && st.w_pending[wb])) issue_w(P, p, sb, wbuf, wb, l, un);
+            if (p.trace && blockIdx.x == 0 && first) p.trace[SF_TRACE_TILE2 + 4 * tp + 2] = clock64();
             st.w_pending[wb] = 0;
-            if (!(first && st.a_pending)) issue_a(P, sb, abuf, un);
-            st.a_pending = 0;
+            issue_a(P, sb, abuf, un);
             const bool tr = p.trace && blockIdx.x == 0 && first;
             if (tr) p.trace[SF_TRACE_TILE + 4 * tp] = clock64();
             bool ok = tc::mbar_wait(&sb->w_full[wb], st.w_uses[wb] & 1u);
@@ -359,8 +353,8 @@ __device__ SF_NI bool tile_phase(const SfParams& P, const SfHot& p, SfBars* sb, 
     }
     // prefetch the weights of this CTA's first unit of the next tile phase
     if (threadIdx.x == 0 && tp + 1 < 4 * p.L) {
-        Unit nx;
-        if (unit_at(p, tp + 1, blockIdx.x, nx)) {
+        if (sb->has_first[(tp + 1) & 3]) {
+            const Unit& nx = sb->first[(tp + 1) & 3];
             const int nb = (tp + 1) & 1;
             issue_w(P, p, sb, smem + SF_A_BYTES + nb * SF_W_BYTES, nb, (tp + 1) >> 2, nx);
             tc::prefetch_tmap(&P.amap[nx.amap]);
@@ -610,8 +604,9 @@ template <int EPL> struct SfKs {
 // Each row phase reads (1) inputs that no phase of this step writes before it
 // (carried state, parameters, rows written two or more barriers earlier) and
 // (2) the partial sums of the tile phase just before it.  The *In structs
-// hold (1); the main loop loads them for a group's first row before the
-// barrier that opens the phase, so their latency overlaps the barrier wait.
+// hold (1) and are loaded at the start of the phase, beside the loads of (2).
+// (Loading them before the opening barrier was measured slower: the
+// arriving thread's release then waits for its own outstanding loads.)
 
 template <int EPL>
 struct WkvIn {
@@ -856,12 +851,13 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     tc::fence_after_sync();
     const uint32_t tmem = sb->tmem_base;
 
-    SfState st{{0, 0}, 0, 0, {0, 0}, 0};
+    SfState st{{0, 0}, 0, 0, {0, 0}};
     // weights of the first tile phase, fetched while the embedding runs
     if (threadIdx.x == 0) {
-        Unit u0;
-        if (unit_at(p, 0, blockIdx.x, u0)) {
-            issue_w(P, p, sb, smem + SF_A_BYTES, 0, 0, u0);
+        // (the other threads read the table after the first grid barrier)
+        for (int k = 0; k < 4; ++k) sb->has_first[k] = unit_at(p, k, blockIdx.x, sb->first[k]);
+        if (sb->has_first[0]) {
+            issue_w(P, p, sb, smem + SF_A_BYTES, 0, 0, sb->first[0]);
             st.w_pending[0] = 1;
         }
     }
@@ -877,31 +873,30 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     unsigned epoch = 0;
     bool ok = true;
     for (int b = gw; b < p.B; b += nw) row_embed<EPL>(grp, p, b);
-    ok = grid_sync(P, p, sb, smem, ++epoch, 0, st);
-// a row phase: inputs of the group's first row loaded before the barrier
+    ok = grid_sync(p, sb, ++epoch);
+// a row phase after its opening barrier, one row per group at a time
 #define SF_ROWS(IN, FN)                                                  \
     {                                                                    \
         IN<EPL> in;                                                      \
-        if (SF_PREROW && gw < p.B) in.load(grp, p, l, gw);               \
-        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, -1, st))) break;   \
+        if (!(ok = grid_sync(p, sb, ++epoch))) break;                   \
         for (int b = gw; b < p.B; b += nw) {                             \
-            if (!SF_PREROW || b != gw) in.load(grp, p, l, b);            \
+            in.load(grp, p, l, b);                                       \
             FN<EPL>(grp, p, l, b, in);                                   \
         }                                                                \
     }
     for (int l = 0; l < p.L && ok; ++l) {
         tile_phase(P, p, sb, smem, tmem, 4 * l + 0, st);
         SF_ROWS(WkvIn, row_wkv)
-        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 1, st))) break;
+        if (!(ok = grid_sync(p, sb, ++epoch))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 1, st);
         SF_ROWS(AttIn, row_att_out)
-        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 2, st))) break;
+        if (!(ok = grid_sync(p, sb, ++epoch))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 2, st);
         SF_ROWS(MidIn, row_ffn_mid)
-        if (!(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * l + 3, st))) break;
+        if (!(ok = grid_sync(p, sb, ++epoch))) break;
         tile_phase(P, p, sb, smem, tmem, 4 * l + 3, st);
         SF_ROWS(OutIn, row_ffn_out)
-        if (l + 1 < p.L && !(ok = grid_sync(P, p, sb, smem, ++epoch, 4 * (l + 1), st))) break;
+        if (l + 1 < p.L && !(ok = grid_sync(p, sb, ++epoch))) break;
     }
 #undef SF_ROWS
     // a prefetched weight load that no phase consumed (abort) must land
@@ -909,7 +904,6 @@ __global__ void __launch_bounds__(SF_NT, 1) k_step_fused(const __grid_constant__
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; ++i)
             if (st.w_pending[i]) tc::mbar_wait(&sb->w_full[i], st.w_uses[i] & 1u);
-        if (st.a_pending) tc::mbar_wait(&sb->a_full, st.a_uses & 1u);
     }
     tc::fence_before_sync();
     __syncthreads();

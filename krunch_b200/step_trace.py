@@ -63,6 +63,14 @@ def main() -> None:
           "landed->MMA done MMA->stored")
     for k, nm in enumerate(["kvr", "o", "ffn", "fv"]):
         print(f"  {nm:4s}", np.round(acc[k] / L, 2))
+    t2 = np.zeros((4, 3))
+    for tp in range(4 * L):
+        st0 = t[768 + 2 * tp + 1]
+        x0, x1, x2 = t[1536 + 4 * tp:1536 + 4 * tp + 3]
+        t2[tp % 4] += np.array([x0 - st0, x1 - x0, x2 - x1]) / 1e3
+    print("tile phase start (k SM cycles): barrier exit->phase entry, ->unit found, ->W issued")
+    for k, nm in enumerate(["kvr", "o", "ffn", "fv"]):
+        print(f"  {nm:4s}", np.round(t2[k] / L, 2))
     print("row phases (k SM cycles, mean over layers): barrier exit->entry entry->data "
           "data->reduced reduced->end")
     racc = np.zeros((4, 4))
