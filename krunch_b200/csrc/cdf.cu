@@ -554,6 +554,7 @@ __global__ void __launch_bounds__(CDF_NT) k_cdf(const uint16_t* __restrict__ log
     const uint16_t* x = logits + (int64_t)row * stride;
     const int nsub = (V + SUBTILE - 1) / SUBTILE;
     const float scale = (float)((1 << bits) - V);
+
     int sym = 0;
     if (MODE == MODE_LOHI) {
         sym = symbols[row];

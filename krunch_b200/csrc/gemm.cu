@@ -94,6 +94,7 @@ extern "C" int kb_gemm_kvr(int dtype, const void* kx, const void* vx, const void
 
 extern "C" int kb_device_error_status(int reset) {
     const int e = kb::read_tc_error(reset);
-    if (e < 0) return KB_ERR_CUDA;
-    return e ? KB_ERR_TIMEOUT : KB_OK;
+    const int f = kb::read_ln_error(reset);
+    if (e < 0 || f < 0) return KB_ERR_CUDA;
+    return (e || f) ? KB_ERR_TIMEOUT : KB_OK;
 }

@@ -440,6 +440,17 @@ __global__ void __launch_bounds__(TC_NT, 1)
                     if (PAIR && rank != 0) tc::mbar_wait(&bars->empty[s], (issued_parity >> s) & 1u);
                     else tc::mbar_wait(&bars->full[s], (issued_parity >> s) & 1u);
                 }
+            // After an abort the leader may never consume (or see land) what
+            // rank 1 loaded into its own shared memory: rank 1 then keeps its
+            // shared memory alive for a bounded 100 us, far beyond a tile
+            // load's flight time, before it may leave.
+            if (PAIR && rank != 0 && tc_aborted(bars)) {
+                unsigned long long t0, t1;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+                do {
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+                } while (t1 - t0 < 100000ull);
+            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer (a pair's leader) ----------------

@@ -6,11 +6,17 @@
 // the carried state, so a window of T rows produces exactly the bits of T
 // single-row steps.  That is what lets the stepped decoder reproduce the
 // packed encoder's logits bit for bit.
+#include <atomic>
+
 #include "kb_common.cuh"
 #include "quant.cuh"
 #include "rwkv_dev.cuh"
 #include "rwkv_ops.cuh"
+#include "tc_common.cuh"
 
+#ifndef KB_LN_TILE
+#define KB_LN_TILE 1  // tiled LN + mix kernel (bulk-copied row tiles) for fp16 / bf16 outputs
+#endif
 #ifndef KB_LN_H2
 #define KB_LN_H2 1  // packed LN + mix kernel for fp16 / bf16 outputs
 #endif
@@ -748,6 +754,219 @@ int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, 
     return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// LayerNorm + token-shift mix over tiles of consecutive rows (fp16 / bf16
+// outputs, C = 32 EPL <= 1024).  A tile's rows are contiguous in memory, so
+// one 1-D bulk copy brings them (and the row before the tile) into shared
+// memory; a persistent CTA double-buffers its tiles on an mbarrier, so the
+// next tile streams in while this one is computed.  Phase 1: each warp takes
+// row pairs and computes their LayerNorm exactly as ln_warp_h2x2 does (same
+// lane order and butterfly: the bits of k_ln_mix_h2), writing the fp16
+// result back in place; warp 0 also normalises the row before the tile when
+// the tile's first row takes its token-shift input from it.  Phase 2: the
+// mixes, one 16-byte chunk per thread at a time, coalesced across the CTA.
+// ---------------------------------------------------------------------------
+#ifndef KB_LNT_RT
+#define KB_LNT_RT 16
+#endif
+#ifndef KB_LNT_CAP
+#define KB_LNT_CAP 8
+#endif
+constexpr int LNT_WARPS = 8;
+__device__ int g_ln_error = 0;
+
+template <int EPL>
+struct LnTile {
+    static constexpr int C = 32 * EPL;
+    static constexpr int RT = EPL <= 24 ? KB_LNT_RT : KB_LNT_RT / 2;  // rows per tile
+    static constexpr uint32_t ROW = (uint32_t)C * 2;     // bytes per fp16 row
+    static constexpr uint32_t BUF = (RT + 1) * ROW;      // slot 0: the row before
+    static constexpr size_t SMEM = 2 * BUF + 64 + 128;   // two buffers + barriers + align
+};
+
+template <int NMIX, int EPL>
+__global__ void __launch_bounds__(LNT_WARPS * 32)
+    k_ln_mix_tile(const uint16_t* __restrict__ x, int B, int T, const float* __restrict__ lw,
+                  const float* __restrict__ lb, MixArgs ma, const float* __restrict__ state_in,
+                  float* __restrict__ state_out, uint16_t* __restrict__ xx_out) {
+    using L = LnTile<EPL>;
+    constexpr int C = L::C, RT = L::RT, H = EPL / 2, CH = C / 8;
+    extern __shared__ unsigned char lnt_raw[];
+    unsigned char* smem = lnt_raw + ((128u - (tc::smem_addr(lnt_raw) & 127u)) & 127u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * L::BUF);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t rows = (int64_t)B * T;
+    const int64_t tiles = (rows + RT - 1) / RT;
+    if ((int64_t)blockIdx.x >= tiles) return;
+    // rows [r0 - 1, r0 + n) of tile `tile` into buffer `bi` (slot 0 = r0 - 1)
+    auto issue = [&](int64_t tile, int bi) {
+        const int64_t r0 = tile * RT;
+        const int64_t n = rows - r0 < RT ? rows - r0 : RT;
+        const int64_t first = r0 > 0 ? r0 - 1 : 0;
+        const uint32_t bytes = (uint32_t)((r0 + n - first) * L::ROW);
+        unsigned char* dst = smem + bi * L::BUF + (r0 > 0 ? 0 : L::ROW);
+        tc::mbar_expect_tx(&full[bi], bytes);
+        tc::bulk_load(dst, x + first * C, bytes, &full[bi]);
+    };
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&full[0], 1);
+        tc::mbar_init(&full[1], 1);
+        tc::fence_barrier_init();
+        issue(blockIdx.x, 0);
+    }
+    __syncthreads();
+    int it = 0;
+    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+        const int bi = it & 1;
+        if (threadIdx.x == 0 && tile + gridDim.x < tiles) {
+            tc::fence_proxy_async_smem();  // this buffer's generic accesses (two tiles ago)
+            issue(tile + gridDim.x, bi ^ 1);
+        }
+        if (!tc::mbar_wait(&full[bi], (uint32_t)(it >> 1) & 1u)) {
+            // bounded wait expired: report, let the other buffer's copy (if
+            // any) land, and leave
+            if (threadIdx.x == 0) {
+                atomicExch(&g_ln_error, 1);
+                if (tile + gridDim.x < tiles) tc::mbar_wait(&full[bi ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
+            }
+            return;
+        }
+        unsigned char* buf = smem + bi * L::BUF;
+        const int64_t r0 = tile * RT;
+        const int n = (int)(rows - r0 < RT ? rows - r0 : RT);
+        const bool need_prev = NMIX > 0 && r0 > 0 && (r0 % T) != 0;
+        // ---- phase 1: LayerNorm of each row, in place -----------------------
+        for (int pr = warp; pr < (n + 1) / 2; pr += LNT_WARPS) {
+            uint32_t* ra = reinterpret_cast<uint32_t*>(buf + (1 + 2 * pr) * L::ROW);
+            uint32_t* rb = reinterpret_cast<uint32_t*>(buf + (2 + 2 * pr) * L::ROW);
+            const bool hasb = 2 * pr + 1 < n;
+            uint32_t va[H], vb[H], oa[H], ob[H];
+#pragma unroll
+            for (int j = 0; j < EPL / 8; ++j) {
+                const uint4 qa = reinterpret_cast<const uint4*>(ra)[j * 32 + lane];
+                va[4 * j] = qa.x; va[4 * j + 1] = qa.y; va[4 * j + 2] = qa.z; va[4 * j + 3] = qa.w;
+                uint4 qb = make_uint4(0u, 0u, 0u, 0u);
+                if (hasb) qb = reinterpret_cast<const uint4*>(rb)[j * 32 + lane];
+                vb[4 * j] = qb.x; vb[4 * j + 1] = qb.y; vb[4 * j + 2] = qb.z; vb[4 * j + 3] = qb.w;
+            }
+            ln_warp_h2x2<EPL>(va, vb, C, lane, lw, lb, oa, ob);
+#pragma unroll
+            for (int j = 0; j < EPL / 8; ++j) {
+                reinterpret_cast<uint4*>(ra)[j * 32 + lane] =
+                    make_uint4(oa[4 * j], oa[4 * j + 1], oa[4 * j + 2], oa[4 * j + 3]);
+                if (hasb)
+                    reinterpret_cast<uint4*>(rb)[j * 32 + lane] =
+                        make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
+            }
+        }
+        if (need_prev && warp == (((n + 1) / 2) % LNT_WARPS)) {  // the least loaded warp
+            uint32_t* rp = reinterpret_cast<uint32_t*>(buf);
+            uint32_t vp[H], op[H];
+#pragma unroll
+            for (int j = 0; j < EPL / 8; ++j) {
+                const uint4 q = reinterpret_cast<const uint4*>(rp)[j * 32 + lane];
+                vp[4 * j] = q.x; vp[4 * j + 1] = q.y; vp[4 * j + 2] = q.z; vp[4 * j + 3] = q.w;
+            }
+            ln_warp_h2<EPL>(vp, C, lane, lw, lb, op);
+#pragma unroll
+            for (int j = 0; j < EPL / 8; ++j)
+                reinterpret_cast<uint4*>(rp)[j * 32 + lane] =
+                    make_uint4(op[4 * j], op[4 * j + 1], op[4 * j + 2], op[4 * j + 3]);
+        }
+        __syncthreads();
+        // ---- phase 2: token-shift mixes, xx / state outputs --------------------
+        for (int q = threadIdx.x; q < n * CH; q += LNT_WARPS * 32) {
+            const int r = q / CH, ch = q - r * CH;
+            const int64_t g = r0 + r;
+            const int b = (int)(g / T), t = (int)(g - (int64_t)b * T);
+            const uint4 cq = reinterpret_cast<const uint4*>(buf + (1 + r) * L::ROW)[ch];
+            const uint32_t cu[4] = {cq.x, cq.y, cq.z, cq.w};
+            if (NMIX > 0) {
+                float pf[8];
+                if (t == 0) {
+                    if (state_in) {
+                        const float4* p4 = reinterpret_cast<const float4*>(state_in + (int64_t)b * C) + 2 * ch;
+                        const float4 a = p4[0], c = p4[1];
+                        pf[0] = a.x; pf[1] = a.y; pf[2] = a.z; pf[3] = a.w;
+                        pf[4] = c.x; pf[5] = c.y; pf[6] = c.z; pf[7] = c.w;
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) pf[k] = 0.0f;
+                    }
+                } else {
+                    const uint4 pq = reinterpret_cast<const uint4*>(buf + r * L::ROW)[ch];
+                    const uint32_t pu[4] = {pq.x, pq.y, pq.z, pq.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = h2f2(pu[k]);
+                        pf[2 * k] = f.x;
+                        pf[2 * k + 1] = f.y;
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < NMIX; ++m) {
+                    const float4* m4 = reinterpret_cast<const float4*>(ma.mix[m]) + 2 * ch;
+                    const float4 m0 = __ldg(m4), m1 = __ldg(m4 + 1);
+                    const float mk[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+                    uint32_t o[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float2 f = h2f2(cu[k]);
+                        const float k0 = mk[2 * k], k1 = mk[2 * k + 1];
+                        const float a0 = __fmaf_rn(f.x, k0, __fmul_rn(pf[2 * k], __fsub_rn(1.0f, k0)));
+                        const float a1 = __fmaf_rn(f.y, k1, __fmul_rn(pf[2 * k + 1], __fsub_rn(1.0f, k1)));
+                        o[k] = ma.bf16 ? f2bf2(a0, a1) : f2h2(a0, a1);
+                    }
+                    reinterpret_cast<uint4*>(ma.out[m] + g * C)[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            if (xx_out) {
+                uint4 o;
+                if (ma.bf16) {
+                    const float2 a = h2f2(cu[0]), c = h2f2(cu[1]), d = h2f2(cu[2]), e = h2f2(cu[3]);
+                    o = make_uint4(f2bf2(a.x, a.y), f2bf2(c.x, c.y), f2bf2(d.x, d.y), f2bf2(e.x, e.y));
+                } else {
+                    o = cq;
+                }
+                reinterpret_cast<uint4*>(xx_out + g * C)[ch] = o;
+            }
+            if (state_out && t == T - 1) {
+                float4* s4 = reinterpret_cast<float4*>(state_out + (int64_t)b * C) + 2 * ch;
+                const float2 a = h2f2(cu[0]), c = h2f2(cu[1]), d = h2f2(cu[2]), e = h2f2(cu[3]);
+                s4[0] = make_float4(a.x, a.y, c.x, c.y);
+                s4[1] = make_float4(d.x, d.y, e.x, e.y);
+            }
+        }
+        __syncthreads();  // the buffer is refilled two tiles on
+    }
+}
+
+template <int NMIX, int EPL>
+int launch_ln_tile(int B, int T, cudaStream_t st, const uint16_t* x, const float* lw,
+                   const float* lb, const MixArgs& ma, const float* state_in, float* state_out,
+                   uint16_t* xx_out) {
+    using L = LnTile<EPL>;
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t e = once_per_device(done, [] {
+        return cudaFuncSetAttribute(k_ln_mix_tile<NMIX, EPL>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::SMEM);
+    });
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return KB_ERR_CUDA;
+    }
+    const int64_t tiles = ((int64_t)B * T + L::RT - 1) / L::RT;
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int per_sm = (int)(220000 / L::SMEM) > 0 ? (int)(220000 / L::SMEM) : 1;
+    const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * (per_sm < KB_LNT_CAP ? per_sm : KB_LNT_CAP);
+    const int grid = (int)(tiles < cap ? tiles : cap);
+    k_ln_mix_tile<NMIX, EPL><<<grid, LNT_WARPS * 32, L::SMEM, st>>>(x, B, T, lw, lb, ma, state_in,
+                                                                   state_out, xx_out);
+    return KB_OK;
+}
+
 template <int NMIX>
 static int ln_mix_epl(int epl, int blocks, int rpw, cudaStream_t st, const uint16_t* x, int B, int T, int C,
                       const float* lw, const float* lb, const MixArgs& ma, const float* state_in,
@@ -787,6 +1006,27 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
         return launch_status();
     }
     const bool quant = ma.q[0] || ma.q[1] || ma.q[2];
+    if (KB_LN_TILE && !quant && epl % 8 == 0 && epl <= 32) {
+#define KB_LNT_CASE(N, E)                                                                       \
+    case E:                                                                                     \
+        rc = launch_ln_tile<N, E>(B, T, st, x, lw, lb, ma, state_in, state_out, xx_out);        \
+        break;
+#define KB_LNT_NMIX(N)                                                                          \
+    case N:                                                                                     \
+        switch (epl) {                                                                          \
+            KB_LNT_CASE(N, 8) KB_LNT_CASE(N, 16) KB_LNT_CASE(N, 24) KB_LNT_CASE(N, 32)          \
+            default: return KB_ERR_SHAPE;                                                       \
+        }                                                                                       \
+        break;
+        switch (nmix) {
+            KB_LNT_NMIX(0) KB_LNT_NMIX(2) KB_LNT_NMIX(3)
+            default: return KB_ERR_ARG;
+        }
+#undef KB_LNT_NMIX
+#undef KB_LNT_CASE
+        if (rc != KB_OK) return rc;
+        return launch_status();
+    }
     if (KB_LN_H2 && !quant && epl % 8 == 0 && epl <= 32) {
 #define KB_LNH_CASE(N, E)                                                                       \
     case E:                                                                                     \
@@ -833,6 +1073,16 @@ int launch_wkv(int conv, int B, int T, int C, const float* k, const float* v, co
     }
 #undef KB_WKV
     return launch_status();
+}
+
+int read_ln_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_ln_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(g_ln_error, &z, sizeof(int));
+    }
+    return v;
 }
 
 int launch_state_init(float* st, int L, int B, int C, cudaStream_t s) {

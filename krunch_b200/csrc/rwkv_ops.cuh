@@ -70,5 +70,7 @@ int launch_gemm_kvr(int kind, const void* const (&A)[3], int64_t lda,
 int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, cudaStream_t st);
 // Device-side error code of the tcgen05 kernels (0 = none); optionally reset.
 int read_tc_error(int reset);
+// The same for the bulk-copy LayerNorm kernel's bounded waits.
+int read_ln_error(int reset);
 
 }  // namespace kb
