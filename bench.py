@@ -247,7 +247,9 @@ def bench_box(args, rank, world, dev, max_over_ranks, barrier):
     raw = log_lines(args.box_chunks * world * cb, seed=4)
     eng = inference.engine
     eng.load(CodecConfig(family="169m", cdf_bits=args.cdf_bits, wdtype="i8"), ByteTokenizer(), dev)
-    eng.compress_chunks_batched([raw[:4096]] * 2)  # warm-up: model, plans, graphs
+    # warm-up, untimed: model, plans, graphs, and the gather's NCCL
+    # peer-to-peer connections (set up on first use)
+    kd.gather_payloads(eng.compress_chunks_batched([raw[:4096]] * 2), 2 * world)
     chunks = chunking.split(raw, chunk_size=cb)
     mine = [chunks[i] for i in kd.shard(len(chunks), rank, world)]
     torch.cuda.synchronize()
