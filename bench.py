@@ -23,6 +23,8 @@ on rank 0 with all host threads.
 Multi-GPU: one process per GPU (torchrun); each rank compresses its own 64
 chunks (weak scaling, no data-path collective).
 
+stress_1b5 : BASELINE configs[4] (RWKV-4 1.5B architecture): bf16 compress
+        B=512 x T=2048 and w8a8 decompress B=512 x 1024 steps per GPU.
 box   : BASELINE configs[3] on a bounded slice (--box-chunks 1 MiB log-line
         chunks per GPU): chunk i on rank i mod G through the engine's batch
         API with the w8a8 model, then the NCCL length all-gather + payload
@@ -288,6 +290,87 @@ def bench_box(args, rank, world, dev, max_over_ranks, barrier):
             "timing": "host perf_counter around device-synchronised steps, max over ranks"}
 
 
+def bench_stress(args, rank, world, dev, max_over_ranks, barrier):
+    """the RWKV-4 1.5B architecture (24 x 2048, FFN 8192),
+    random-init weights drawn on the device (synth.random_weights_device).
+    Compress: bf16 weights, B chunks x T tokens, W warm-up steps then K timed
+    steps (CUDA events).  Decompress: w8a8 weights, B streams stepped for
+    dec_T steps (per-op kernels: the fused step is sized for 169M), streams
+    compressed first by the same model; byte-exactness checked."""
+    import torch
+    from krunch_b200.codec import Codec, CompressPlan, DecompressPlan
+    from krunch_b200.model import RWKVModel
+    from krunch_b200.synth import random_weights_device, zipf_tokens
+    sh = SHAPES["1.5b"]
+    C, F, L, V = sh["n_embd"], sh["n_ffn"], sh["n_layer"], sh["n_vocab"]
+    w = random_weights_device(**sh, seed=0, device=dev)
+    pk, pk_kind = peaks()
+    out = {"workload": f"configs[4] 1.5B stress: compress bf16 B={args.stress_B} x "
+                       f"T={args.stress_T}, decompress w8a8 B={args.stress_B} x "
+                       f"{args.stress_dec_T} steps, per GPU"}
+    # ---- compress, bf16 ----
+    model = RWKVModel(w, device=dev, wdtype="bf16")
+    codec = Codec(model, cdf_bits=args.cdf_bits)
+    B, T = args.stress_B, args.stress_T
+    seqs = list(zipf_tokens((B, T), seed=200 + rank))
+    plan = CompressPlan(codec, [T] * B)
+    plan.upload(seqs)
+    for _ in range(args.warmup):
+        plan.run()
+    torch.cuda.synchronize()
+    barrier()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.stress_steps):
+            plan.run()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.stress_steps)
+    flop_tok = 2.0 * (L * (5 * C * C + 2 * C * F) + C * V)
+    tf = B * T * flop_tok / (ms / 1e3) / 1e12
+    out["compress"] = {"value": B * T * world * BYTES_PER_TOKEN / (ms / 1e3) / 1e6, "unit": "MB/s",
+                       "ms_per_step": ms, "steps": args.stress_steps, "warmup": args.warmup,
+                       "dtype": "bf16", "achieved_tflops": tf,
+                       "frac_of_sustained_bf16": tf / pk["bf16_tflops_sustained"],
+                       "peak_kind": pk_kind, "clocks": clk.summary()}
+    del plan, codec, model
+    torch.cuda.empty_cache()
+    # ---- decompress, w8a8 ----
+    model = RWKVModel(w, device=dev, wdtype="i8")
+    del w
+    codec = Codec(model, cdf_bits=args.cdf_bits)
+    Td = args.stress_dec_T
+    seqs = list(zipf_tokens((B, Td), seed=300 + rank))
+    streams = codec.compress_tokens(seqs)
+    lens = [len(s) for s in streams]
+    dp = DecompressPlan(codec, lens, [Td] * B)
+    dp.upload(streams)
+    dp.run()  # warm-up, graph capture
+    torch.cuda.synchronize()
+    dp2 = DecompressPlan(codec, lens, [Td] * B)
+    dp2.upload(streams)
+    torch.cuda.synchronize()
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(stream)
+    dp2.run()
+    d1.record(stream)
+    torch.cuda.synchronize()
+    dms = max_over_ranks(d0.elapsed_time(d1))
+    ok = all(np.array_equal(a, b) for a, b in zip(dp2.fetch(), seqs))
+    w_bytes = L * (5 * C * C + 2 * C * F) + C * V
+    us = dms * 1e3 / Td
+    ach = (w_bytes + 2 * L * 5 * B * C * 4) / (us * 1e-6) / 1e9
+    out["decompress"] = {"value": B * Td * world * BYTES_PER_TOKEN / (dms / 1e3) / 1e6,
+                         "unit": "MB/s", "us_per_step": us, "byte_exact": bool(ok),
+                         "hbm_frac": ach / pk["hbm_gbs"], "peak_kind": pk_kind}
+    del dp, dp2, codec, model
+    torch.cuda.empty_cache()
+    return out
+
+
 def config(args):
     name = "RWKV-4-169M" if args.model == "169m" else "RWKV-4 1.5B architecture"
     wl = ("configs[1] compress, packed forward, 1 GPU per rank" if args.model == "169m"
@@ -325,6 +408,12 @@ def main():
                     help="skip the configs[3] slice (log lines, 1 MiB chunks, NCCL stitch)")
     ap.add_argument("--box-chunks", type=int, default=8, help="1 MiB chunks per GPU")
     ap.add_argument("--box-chunk-bytes", type=int, default=1 << 20)
+    ap.add_argument("--no-stress", action="store_true",
+                    help="skip the configs[4] 1.5B stress lines")
+    ap.add_argument("--stress-B", type=int, default=512)
+    ap.add_argument("--stress-T", type=int, default=2048)
+    ap.add_argument("--stress-steps", type=int, default=1)
+    ap.add_argument("--stress-dec-T", type=int, default=1024)
     args = ap.parse_args()
     global SHAPE
     SHAPE = SHAPES[args.model]
@@ -459,6 +548,8 @@ def main():
 
     if not args.no_box:
         extra["box"] = bench_box(args, rank, world, dev, max_over_ranks, barrier)
+    if not args.no_stress and args.model == "169m":
+        extra["stress_1b5"] = bench_stress(args, rank, world, dev, max_over_ranks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -43,7 +43,6 @@
 
 namespace kb {
 
-
 constexpr int SF_NT = 256;                       // 8 warps
 constexpr int SF_BN = 64;                        // N columns per unit
 constexpr int SF_MAX_KB = 6;                     // 128-byte K blocks per unit

@@ -66,6 +66,44 @@ def random_weights(n_layer: int, n_embd: int, n_ffn: int, n_vocab: int, seed: in
     return w
 
 
+def random_weights_device(n_layer: int, n_embd: int, n_ffn: int, n_vocab: int, seed: int = 0,
+                          std: float = 0.02, device="cuda") -> dict[str, np.ndarray]:
+    """The distribution of ``random_weights`` drawn by torch's generator on a
+    CUDA device (seconds instead of minutes for the 1.5B shapes), returned
+    as numpy float32 arrays in the same layout.  A different stream of
+    numbers than ``random_weights`` for the same seed."""
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    C, F, V = n_embd, n_ffn, n_vocab
+
+    def normal(*shape):
+        return (torch.randn(shape, generator=g, device=device) * std).cpu().numpy()
+
+    def unif(lo, hi, n):
+        return (torch.rand(n, generator=g, device=device) * (hi - lo) + lo).cpu().numpy()
+
+    w: dict[str, np.ndarray] = {"emb.weight": normal(V, C)}
+    ones, zeros = np.ones(C, np.float32), np.zeros(C, np.float32)
+    for i in range(n_layer):
+        b, att, ffn = f"blocks.{i}.", f"blocks.{i}.att.", f"blocks.{i}.ffn."
+        w[b + "ln1.weight"], w[b + "ln1.bias"] = ones.copy(), zeros.copy()
+        w[b + "ln2.weight"], w[b + "ln2.bias"] = ones.copy(), zeros.copy()
+        w[att + "time_decay"] = unif(-5.0, 0.0, C)
+        w[att + "time_first"] = unif(-1.0, 1.0, C)
+        for n in ("time_mix_k", "time_mix_v", "time_mix_r"):
+            w[att + n] = unif(0.0, 1.0, C)
+        for n in ("key", "value", "receptance", "output"):
+            w[att + n + ".weight"] = normal(C, C)
+        w[ffn + "time_mix_k"] = unif(0.0, 1.0, C)
+        w[ffn + "time_mix_r"] = unif(0.0, 1.0, C)
+        w[ffn + "key.weight"] = normal(C, F)
+        w[ffn + "value.weight"] = normal(F, C)
+        w[ffn + "receptance.weight"] = normal(C, C)
+    w["ln_out.weight"], w["ln_out.bias"] = ones.copy(), zeros.copy()
+    w["head.weight"] = normal(C, V)
+    return w
+
+
 def zipf_tokens(shape, vocab: int = 50277, s: float = 1.1, seed: int = 0) -> np.ndarray:
     rng = np.random.default_rng(seed)
     ranks = np.arange(1, vocab + 1, dtype=np.float64)
