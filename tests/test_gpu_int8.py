@@ -170,7 +170,8 @@ def test_i8_codec_roundtrip(torch):
 
 @pytest.mark.parametrize("shape,B", [((2, 128, 512, 300), 3), ((2, 128, 512, 300), 300),
                                      ((2, 2048, 8192, 300), 5),
-                                     ((12, 768, 3072, 50277), 256), ((12, 768, 3072, 50277), 5)])
+                                     ((12, 768, 3072, 50277), 256), ((12, 768, 3072, 50277), 5),
+                                     ((12, 768, 3072, 50277), 600), ((12, 768, 3072, 50277), 1184)])
 def test_fused_step_matches_window_forward(torch, shape, B):
     """kb_step_forward (one persistent launch per step) == kb_forward_window
     with T = 1, bit for bit, logits, softmax partials and state, over

@@ -150,3 +150,19 @@ def test_cli_roundtrip_and_corruption(torch, tiny_env, tmp_path):
     bad.write_bytes(bytes(data))
     r = run("decompress", "--in", str(bad), "--out", str(tmp_path / "x"))
     assert r.returncode != 0
+
+
+@pytest.mark.parametrize("raw", [b"", b"\x00", b"a", "\u20ac".encode()])
+def test_cli_tiny_inputs(torch, tiny_env, tmp_path, raw):
+    """Empty and one-byte inputs through the CLI (0 chunks / 1 chunk of one
+    token): the blob round-trips, length and CRC checked on the way back."""
+    src, blob, back = tmp_path / "in", tmp_path / "blob", tmp_path / "out"
+    src.write_bytes(raw)
+    env = dict(os.environ, PYTHONPATH=REPO)
+    run = lambda *a: subprocess.run([sys.executable, "-m", "krunch_b200.cli", *a], env=env,  # noqa
+                                    capture_output=True, timeout=600)
+    r = run("compress", "--in", str(src), "--out", str(blob))
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    r = run("decompress", "--in", str(blob), "--out", str(back))
+    assert r.returncode == 0, r.stderr.decode()[-2000:]
+    assert back.read_bytes() == raw
