@@ -206,6 +206,30 @@ def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
     torch.cuda.synchronize()
     ems = max_over_ranks(e0.elapsed_time(e1))
     ok = ok and all(np.array_equal(a, b) for a, b in zip(out, seqs))
+    # the same decode at the engine's default batch (compute_decompress_batch:
+    # the reference's formula, SMs x 8 = 1184 streams on B200), fewer steps
+    from krunch_b200.codec import compute_decompress_batch
+    Bp, Tp = compute_decompress_batch(-1, stream.device), args.dec_default_T
+    seqs_p = list(zipf_tokens((Bp, Tp), seed=500 + rank))
+    streams_p = codec.compress_tokens(seqs_p)
+    dpp = DecompressPlan(codec, [len(x) for x in streams_p], [Tp] * Bp)
+    dpp.upload(streams_p)
+    dpp.run()  # warm-up, graph capture
+    dpp2 = DecompressPlan(codec, [len(x) for x in streams_p], [Tp] * Bp)
+    dpp2.upload(streams_p)
+    torch.cuda.synchronize()
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    dpp2.run()
+    p1.record(stream)
+    torch.cuda.synchronize()
+    pms = max_over_ranks(p0.elapsed_time(p1))
+    ok_p = all(np.array_equal(a, b) for a, b in zip(dpp2.fetch(), seqs_p))
+    at_default = {"streams": Bp, "steps": Tp, "us_per_step": pms * 1e3 / Tp,
+                  "value": Bp * Tp * world * BYTES_PER_TOKEN / (pms / 1e3) / 1e6, "unit": "MB/s",
+                  "byte_exact": bool(ok_p)}
+    del dpp, dpp2
     sp = SHAPE
     C, F, L, V = sp["n_embd"], sp["n_ffn"], sp["n_layer"], sp["n_vocab"]
     w_bytes = L * (5 * C * C + 2 * C * F) + C * V          # int8 weights read per step
@@ -217,13 +241,14 @@ def bench_decompress(args, rank, world, stream, max_over_ranks, barrier):
     return {"workload": f"configs[2] decompress: w8a8 RWKV-4-169M, B={Bd} x {Td} steps per GPU, "
                         "fp32 state, CUDA graph of (fused step, head, decode) per step",
             "value": tok * BYTES_PER_TOKEN / (dms / 1e3) / 1e6, "unit": "MB/s",
-            "us_per_step": us, "byte_exact": bool(ok), "gpu_launches_per_step": 4,
+            "us_per_step": us, "byte_exact": bool(ok), "gpu_launches_per_step": 3,
             "bits_per_token": 8.0 * sum(lens) / (Bd * Td),
             "roofline": {"bound": "hbm", "achieved": ach, "unit": "GB/s", "peak": pk["hbm_gbs"],
                          "peak_kind": pk_kind, "frac": ach / pk["hbm_gbs"],
                          "algorithmic_bytes_per_step": w_bytes + s_bytes},
             "e2e": {"value": tok * BYTES_PER_TOKEN / (ems / 1e3) / 1e6, "unit": "MB/s",
                     "h2d_bytes_per_step": dp2.h2d_bytes, "d2h_bytes_per_step": dp2.d2h_bytes},
+            "at_default_batch": at_default,
             "clocks": clk.summary()}
 
 
@@ -404,6 +429,8 @@ def main():
                     help="skip the configs[2] decompress line (w8a8, B=256 x 2048 steps)")
     ap.add_argument("--dec-B", type=int, default=256)
     ap.add_argument("--dec-T", type=int, default=2048)
+    ap.add_argument("--dec-default-T", type=int, default=256,
+                    help="steps of the decode at the engine's default batch")
     ap.add_argument("--no-box", action="store_true",
                     help="skip the configs[3] slice (log lines, 1 MiB chunks, NCCL stitch)")
     ap.add_argument("--box-chunks", type=int, default=8, help="1 MiB chunks per GPU")
