@@ -105,6 +105,24 @@ class Codec:
             out.extend(self._compress_group(seqs[i:i + mb]))
         return out
 
+    def compress_batches(self, batches):
+        """Pipelined compress of an iterable of batches (each a list of token
+        sequences): yields each batch's bitstreams in order.  Batch i+1 is
+        planned, uploaded and enqueued while batch i still runs on the GPU;
+        batch i's results come back through pinned memory behind its own
+        launches, so waiting for them does not wait for batch i+1."""
+        prev = None
+        for seqs in batches:
+            plan = CompressPlan(self, [len(s) for s in seqs])
+            plan.upload(seqs)
+            plan.run()
+            plan.fetch_async()
+            if prev is not None:
+                yield prev.fetch()
+            prev = plan
+        if prev is not None:
+            yield prev.fetch()
+
     def _compress_group(self, seqs) -> list[bytes]:
         plan = CompressPlan(self, [len(s) for s in seqs])
         plan.upload(seqs)
@@ -223,9 +241,26 @@ class CompressPlan:
         per_window = 1 + per_layer * L + 2 + 2   # embed, layers, ln_out+head, cdf+encode
         return 2 + self.windows * per_window + 1
 
+    def fetch_async(self) -> None:
+        """Enqueue the copies of the coder states and bitstreams into pinned
+        host memory behind run() on the current stream, and record an event;
+        fetch() then waits for that event only, not for later work."""
+        self._ac_h = torch.empty(self.ac.shape, dtype=self.ac.dtype).pin_memory()
+        self._out_h = torch.empty(self.out_d.shape, dtype=self.out_d.dtype).pin_memory()
+        self._ac_h.copy_(self.ac, non_blocking=True)
+        self._out_h.copy_(self.out_d, non_blocking=True)
+        self._done = torch.cuda.Event()
+        self._done.record(torch.cuda.current_stream(self.codec.dev))
+
     def fetch(self) -> list[bytes]:
-        ac_h = self.ac.view(self.B, 4).cpu().numpy().view(np.uint32)
-        out_h = self.out_d.cpu().numpy()
+        if getattr(self, "_done", None) is not None:
+            self._done.synchronize()
+            ac_h = self._ac_h.numpy().view(np.uint32).reshape(self.B, 4)
+            out_h = self._out_h.numpy()
+            self._done = None
+        else:
+            ac_h = self.ac.view(self.B, 4).cpu().numpy().view(np.uint32)
+            out_h = self.out_d.cpu().numpy()
         self.d2h_bytes = self.ac.numel() * 4 + self.out_d.numel()
         res = []
         for b in range(self.B):

@@ -59,6 +59,21 @@ def _peaked():
     return mod.peaked_weights(), list(np.load(os.path.join(GOLDEN, "peaked_169m_tokens.npy")))
 
 
+def test_compress_batches_pipelined_equals_single(torch):
+    """Codec.compress_batches (batch i+1 prepared and enqueued while batch i
+    runs, results through pinned memory) yields each batch's bytes exactly
+    as compress_tokens does, in order."""
+    from krunch_b200.codec import Codec
+    from krunch_b200.model import RWKVModel
+    codec = Codec(RWKVModel(random_weights(2, 128, 512, 300, seed=3)), cdf_bits=16)
+    rng = np.random.default_rng(7)
+    batches = [[rng.integers(0, 300, n).astype(np.int32) for n in lens]
+               for lens in ((5, 90, 33), (1,), (200, 200), (64, 3, 17, 120))]
+    want = [codec.compress_tokens(b) for b in batches]
+    assert list(codec.compress_batches(batches)) == want
+    assert list(codec.compress_batches([])) == []
+
+
 def _oracle_size(w, seqs, bits, key):
     """Bytes of the CPU oracle pipeline: fp32 forward (oracle/rwkv.py, pinned
     to rwkv4_step_ref) -> CDF rule of krunch_ac/cdf.py:22-74 -> range coder
