@@ -17,15 +17,6 @@
 #ifndef KB_LN_TILE
 #define KB_LN_TILE 1  // tiled LN + mix kernel (bulk-copied row tiles) for fp16 / bf16 outputs
 #endif
-#ifndef KB_LN_H2
-#define KB_LN_H2 1  // packed LN + mix kernel for fp16 / bf16 outputs
-#endif
-#ifndef KB_LN_PF
-#define KB_LN_PF 0  // packed kernel: load the next row pair before computing this one
-#endif
-#ifndef KB_LN_MINB
-#define KB_LN_MINB 2  // resident blocks per SM the packed kernel is compiled for
-#endif
 
 namespace kb {
 
@@ -115,19 +106,6 @@ __device__ __forceinline__ uint32_t f2bf2(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int EPL>
-__device__ __forceinline__ void load_row_h2(const uint16_t* __restrict__ x, int lane,
-                                            uint32_t (&h)[EPL / 2]) {
-#pragma unroll
-    for (int j = 0; j < EPL / 8; ++j) {
-        const uint4 q = __ldg(reinterpret_cast<const uint4*>(x) + j * 32 + lane);
-        h[4 * j] = q.x;
-        h[4 * j + 1] = q.y;
-        h[4 * j + 2] = q.z;
-        h[4 * j + 3] = q.w;
-    }
-}
-
 // ln_warp on a packed row; out = the fp16-rounded LN values, packed
 template <int EPL>
 __device__ __forceinline__ void ln_warp_h2(const uint32_t (&v)[EPL / 2], int C, int lane,
@@ -210,162 +188,6 @@ __device__ __forceinline__ void ln_warp_h2x2(const uint32_t (&va)[EPL / 2],
             ob[4 * j + k] =
                 f2h2(__fmaf_rn(__fmul_rn(__fsub_rn(fb.x, mb), rb), wv[2 * k], bv[2 * k]),
                      __fmaf_rn(__fmul_rn(__fsub_rn(fb.y, mb), rb), wv[2 * k + 1], bv[2 * k + 1]));
-        }
-    }
-}
-
-// 8 token-shift inputs of chunk jj: the carried state (fp32) at t == 0,
-// else the packed LN row before.
-template <int EPL>
-__device__ __forceinline__ void prev_chunk(bool first, const float* st, const uint32_t (&pv)[EPL / 2],
-                                           int jj, int lane, float (&pf)[8]) {
-    if (first) {
-        if (st) {
-            const float4* p4 = reinterpret_cast<const float4*>(st) + (jj * 32 + lane) * 2;
-            const float4 a = p4[0], c = p4[1];
-            pf[0] = a.x; pf[1] = a.y; pf[2] = a.z; pf[3] = a.w;
-            pf[4] = c.x; pf[5] = c.y; pf[6] = c.z; pf[7] = c.w;
-        } else {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) pf[k] = 0.0f;
-        }
-    } else {
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 f = h2f2(pv[4 * jj + k]);
-            pf[2 * k] = f.x;
-            pf[2 * k + 1] = f.y;
-        }
-    }
-}
-
-template <int EPL>
-__device__ __forceinline__ void store_xx(uint16_t* dst, const uint32_t (&cur)[EPL / 2], int lane,
-                                         bool bf) {
-#pragma unroll
-    for (int jj = 0; jj < EPL / 8; ++jj) {
-        uint4 o;
-        if (bf) {
-            const float2 a = h2f2(cur[4 * jj]), c = h2f2(cur[4 * jj + 1]);
-            const float2 d = h2f2(cur[4 * jj + 2]), e = h2f2(cur[4 * jj + 3]);
-            o = make_uint4(f2bf2(a.x, a.y), f2bf2(c.x, c.y), f2bf2(d.x, d.y), f2bf2(e.x, e.y));
-        } else {
-            o = make_uint4(cur[4 * jj], cur[4 * jj + 1], cur[4 * jj + 2], cur[4 * jj + 3]);
-        }
-        reinterpret_cast<uint4*>(dst)[jj * 32 + lane] = o;
-    }
-}
-
-template <int EPL>
-__device__ __forceinline__ void store_state(float* dst, const uint32_t (&cur)[EPL / 2], int lane) {
-#pragma unroll
-    for (int jj = 0; jj < EPL / 8; ++jj) {
-        float4* s4 = reinterpret_cast<float4*>(dst) + (jj * 32 + lane) * 2;
-        const float2 a = h2f2(cur[4 * jj]), c = h2f2(cur[4 * jj + 1]);
-        const float2 d = h2f2(cur[4 * jj + 2]), e = h2f2(cur[4 * jj + 3]);
-        s4[0] = make_float4(a.x, a.y, c.x, c.y);
-        s4[1] = make_float4(d.x, d.y, e.x, e.y);
-    }
-}
-
-// A strip of rpw rows per warp, taken two at a time: rows A = r and
-// B = r + 1 share every parameter load; the next pair is loaded while the
-// current one is computed.  Token shift: A's input is the row before (the
-// previous pair's B, the recomputed LN of row r - 1 at the strip's start, or
-// the carried state at t == 0); B's is A (or the state when B starts a
-// stream).
-template <int NMIX, int EPL>
-__global__ void __launch_bounds__(LN_WARPS * 32, KB_LN_MINB)
-    k_ln_mix_h2(const uint16_t* __restrict__ x, int B, int T, int C, const float* __restrict__ lw,
-                const float* __restrict__ lb, MixArgs ma, const float* __restrict__ state_in,
-                float* __restrict__ state_out, uint16_t* __restrict__ xx_out, int rpw) {
-    static_assert(EPL % 8 == 0, "vector rows");
-    constexpr int H = EPL / 2;
-    const int lane = threadIdx.x & 31;
-    const int64_t rows = (int64_t)B * T;
-    const int64_t r0 = ((int64_t)blockIdx.x * LN_WARPS + (threadIdx.x >> 5)) * rpw;
-    if (r0 >= rows) return;
-    uint32_t va[H], vb[H], na[H], nb[H], ca[H], cb[H], pv[H];
-#pragma unroll
-    for (int i = 0; i < H; ++i) vb[i] = 0u;
-    load_row_h2<EPL>(x + r0 * C, lane, va);
-    if (rpw > 1 && r0 + 1 < rows) load_row_h2<EPL>(x + (r0 + 1) * C, lane, vb);
-    {
-        const int t0 = (int)(r0 % T);
-        if (NMIX > 0 && t0 > 0) {  // the strip's first row: LN of the row before
-            load_row_h2<EPL>(x + (r0 - 1) * C, lane, na);
-            ln_warp_h2<EPL>(na, C, lane, lw, lb, pv);
-        }
-    }
-    for (int j = 0; j < rpw; j += 2) {
-        const int64_t ra = r0 + j, rb = ra + 1;
-        if (ra >= rows) return;
-        const bool hasb = j + 1 < rpw && rb < rows;  // B in this warp's strip
-        const bool more = j + 2 < rpw && ra + 2 < rows;
-        if (KB_LN_PF && more) {
-#pragma unroll
-            for (int i = 0; i < H; ++i) nb[i] = 0u;
-            load_row_h2<EPL>(x + (ra + 2) * C, lane, na);
-            if (j + 3 < rpw && ra + 3 < rows) load_row_h2<EPL>(x + (ra + 3) * C, lane, nb);
-        }
-        const int ba = (int)(ra / T), ta = (int)(ra - (int64_t)ba * T);
-        const int bb = ta + 1 < T ? ba : ba + 1, tb = ta + 1 < T ? ta + 1 : 0;
-        ln_warp_h2x2<EPL>(va, vb, C, lane, lw, lb, ca, cb);
-        if (xx_out) {
-            store_xx<EPL>(xx_out + ra * C, ca, lane, ma.bf16);
-            if (hasb) store_xx<EPL>(xx_out + rb * C, cb, lane, ma.bf16);
-        }
-        const float* sta = state_in ? state_in + (int64_t)ba * C : nullptr;
-        const float* stb = state_in ? state_in + (int64_t)bb * C : nullptr;
-#pragma unroll
-        for (int m = 0; m < NMIX; ++m) {
-#pragma unroll
-            for (int jj = 0; jj < EPL / 8; ++jj) {
-                const float4* m4 = reinterpret_cast<const float4*>(ma.mix[m]) + (jj * 32 + lane) * 2;
-                const float4 m0 = __ldg(m4), m1 = __ldg(m4 + 1);
-                const float mk[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
-                float pa[8], pb[8];
-                prev_chunk<EPL>(ta == 0, sta, pv, jj, lane, pa);
-                prev_chunk<EPL>(tb == 0, stb, ca, jj, lane, pb);
-                uint32_t oa[4], ob[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float2 fa = h2f2(ca[4 * jj + k]), fb = h2f2(cb[4 * jj + k]);
-                    const float k0 = mk[2 * k], k1 = mk[2 * k + 1];
-                    const float i0 = __fsub_rn(1.0f, k0), i1 = __fsub_rn(1.0f, k1);
-                    const float a0 = __fmaf_rn(fa.x, k0, __fmul_rn(pa[2 * k], i0));
-                    const float a1 = __fmaf_rn(fa.y, k1, __fmul_rn(pa[2 * k + 1], i1));
-                    const float b0 = __fmaf_rn(fb.x, k0, __fmul_rn(pb[2 * k], i0));
-                    const float b1 = __fmaf_rn(fb.y, k1, __fmul_rn(pb[2 * k + 1], i1));
-                    oa[k] = ma.bf16 ? f2bf2(a0, a1) : f2h2(a0, a1);
-                    ob[k] = ma.bf16 ? f2bf2(b0, b1) : f2h2(b0, b1);
-                }
-                reinterpret_cast<uint4*>(ma.out[m] + ra * C)[jj * 32 + lane] =
-                    make_uint4(oa[0], oa[1], oa[2], oa[3]);
-                if (hasb)
-                    reinterpret_cast<uint4*>(ma.out[m] + rb * C)[jj * 32 + lane] =
-                        make_uint4(ob[0], ob[1], ob[2], ob[3]);
-            }
-        }
-        if (state_out) {
-            if (ta == T - 1) store_state<EPL>(state_out + (int64_t)ba * C, ca, lane);
-            if (hasb && tb == T - 1) store_state<EPL>(state_out + (int64_t)bb * C, cb, lane);
-        }
-#pragma unroll
-        for (int i = 0; i < H; ++i) pv[i] = cb[i];
-        if (more) {
-            if (KB_LN_PF) {
-#pragma unroll
-                for (int i = 0; i < H; ++i) {
-                    va[i] = na[i];
-                    vb[i] = nb[i];
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < H; ++i) vb[i] = 0u;
-                load_row_h2<EPL>(x + (ra + 2) * C, lane, va);
-                if (j + 3 < rpw && ra + 3 < rows) load_row_h2<EPL>(x + (ra + 3) * C, lane, vb);
-            }
         }
     }
 }
@@ -761,7 +583,7 @@ int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, 
 // memory; a persistent CTA double-buffers its tiles on an mbarrier, so the
 // next tile streams in while this one is computed.  Phase 1: each warp takes
 // row pairs and computes their LayerNorm exactly as ln_warp_h2x2 does (same
-// lane order and butterfly: the bits of k_ln_mix_h2), writing the fp16
+// lane order and butterfly), writing the fp16
 // result back in place; warp 0 also normalises the row before the tile when
 // the tile's first row takes its token-shift input from it.  Phase 2: the
 // mixes, one 16-byte chunk per thread at a time, coalesced across the CTA.
@@ -1025,26 +847,6 @@ int launch_ln_mix(int nmix, const uint16_t* x, int B, int T, int C, const float*
 #undef KB_LNT_NMIX
 #undef KB_LNT_CASE
         if (rc != KB_OK) return rc;
-        return launch_status();
-    }
-    if (KB_LN_H2 && !quant && epl % 8 == 0 && epl <= 32) {
-#define KB_LNH_CASE(N, E)                                                                       \
-    case E:                                                                                     \
-        k_ln_mix_h2<N, E><<<blocks, LN_WARPS * 32, 0, st>>>(x, B, T, C, lw, lb, ma, state_in,   \
-                                                            state_out, xx_out, rpw);            \
-        break;
-#define KB_LNH_NMIX(N)                                                                          \
-    case N:                                                                                     \
-        switch (epl) {                                                                          \
-            KB_LNH_CASE(N, 8) KB_LNH_CASE(N, 16) KB_LNH_CASE(N, 24) KB_LNH_CASE(N, 32)          \
-        }                                                                                       \
-        break;
-        switch (nmix) {
-            KB_LNH_NMIX(0) KB_LNH_NMIX(2) KB_LNH_NMIX(3)
-            default: return KB_ERR_ARG;
-        }
-#undef KB_LNH_NMIX
-#undef KB_LNH_CASE
         return launch_status();
     }
     switch (nmix) {
