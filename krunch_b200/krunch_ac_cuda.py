@@ -223,16 +223,21 @@ _LAYER_CACHE: dict = {}
 
 
 def _layer_handle(w, dev) -> _LayerHandle:
-    key = tuple((t.data_ptr(), tuple(t.shape), t.dtype) for t in w)
+    """The converted layer for these 18 tensors.  The entry holds the source
+    tensors, so their addresses cannot be reused by other tensors while it
+    is cached, and the key includes each tensor's in-place version counter,
+    so an edited tensor is converted again."""
+    key = tuple((t.data_ptr(), tuple(t.shape), t.dtype, t._version) for t in w)
     h = _LAYER_CACHE.get(key)
     if h is None:
         h = _LAYER_CACHE[key] = _LayerHandle(w, dev)
+        h.src = tuple(w)
     return h
 
 
 def clear_layer_graph_cache() -> None:
-    """Drop the cached layer handles (the reference's cache reset,
-    layer_cpp.cpp:1038)."""
+    """Drop the cached layer handles and the tensors they hold (the
+    reference's cache reset, layer_cpp.cpp:1038)."""
     _LAYER_CACHE.clear()
 
 
