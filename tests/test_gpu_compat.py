@@ -185,3 +185,35 @@ def test_cpp_path_packed_equals_stepped_and_cdf(torch):
     assert np.array_equal(cdf.cpu().numpy(), want)
     assert torch.equal(cpp_path.softmax_cdf_one_row(packed[5]), cdf[5])
     assert cpp_path.compute_decompress_batch(5) == 5
+
+
+def test_layer_step_cache_sees_in_place_edits(torch):
+    """The reference-named layer step caches its converted weights; an
+    in-place edit of an input tensor is picked up, a repeated call reuses
+    the entry."""
+    import krunch_ac_cuda
+    from krunch_b200 import _native as N
+    w = _fp16_exact(random_weights(1, 128, 512, 300, seed=15))
+    dev = torch.device("cuda")
+    td = torch.from_numpy(w["blocks.0.att.time_decay"]).to(dev)
+    decay = torch.empty_like(td)
+    N.call("kb_prepare_decay", td.data_ptr(), decay.data_ptr(), td.numel(), N.stream_ptr(dev))
+    layer = _ref_layer_tensors(torch, w, 0, dev, decay)
+    x = (torch.randn((2, 5, 128), device=dev) * 0.1).half()
+
+    def run():
+        s = [torch.zeros(2, 128, dtype=torch.float16, device=dev),
+             torch.zeros(2, 128, device=dev), torch.zeros(2, 128, device=dev),
+             torch.full((2, 128), -1e30, device=dev),
+             torch.zeros(2, 128, dtype=torch.float16, device=dev)]
+        return krunch_ac_cuda.rwkv4_layer_step_cpp(x, *s, *layer)
+
+    krunch_ac_cuda.clear_layer_graph_cache()
+    a = run()
+    b = run()
+    assert torch.equal(a, b) and len(krunch_ac_cuda._LAYER_CACHE) == 1
+    layer[10].mul_(2.0)  # Ow, in place
+    c = run()
+    assert len(krunch_ac_cuda._LAYER_CACHE) == 2 and not torch.equal(a, c)
+    krunch_ac_cuda.clear_layer_graph_cache()
+    assert torch.equal(run(), c)
