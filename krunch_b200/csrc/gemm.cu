@@ -1,5 +1,6 @@
 // Public GEMM entry point (kb_gemm) and the device error report; the kernel
 // itself is the tcgen05 GEMM in gemm_tc.cu.
+#include "profile.cuh"
 #include "rwkv_ops.cuh"
 
 namespace kb {
@@ -23,6 +24,7 @@ extern "C" int kb_gemm_tiled(int dtype, const void* A, int64_t lda, const void* 
     if (!aligned16(A) || !aligned16(W) || (lda % 8) || (ldw % 8) || lda < K || ldw < K ||
         ldo < N || (ldo % 8) || !aligned16(out))
         return KB_ERR_ALIGN;
+    ProfScope ps(PH_GEMM, as_stream(stream), 2.0 * M * (double)N * K);
     if (dtype == KB_BF16)
         return launch_gemm_bf16(reinterpret_cast<const uint16_t*>(A), lda,
                                 reinterpret_cast<const uint16_t*>(W), ldw, M, N, K, epilogue, out,
@@ -55,6 +57,7 @@ extern "C" int kb_gemm_i8(const int8_t* A, int64_t lda, const float* a_scale, co
     if (!aligned16(A) || !aligned16(W) || !aligned16(w_scale) || (lda % 16) || (ldw % 16) ||
         lda < K || ldw < K || ldo < N || (ldo % 8) || !aligned16(out))
         return KB_ERR_ALIGN;
+    ProfScope ps(PH_GEMM, as_stream(stream), 2.0 * M * (double)N * K);
     return launch_gemm_i8(A, lda, a_scale, W, ldw, w_scale, M, N, K, epilogue, out, ldo, resid,
                           gate, as_stream(stream), tile_n);
 }
@@ -88,6 +91,7 @@ extern "C" int kb_gemm_kvr(int dtype, const void* kx, const void* vx, const void
     const float* const as[3] = {kx_scale, vx_scale, rx_scale};
     const uint16_t* const ws[3] = {kw_scale, vw_scale, rw_scale};
     void* const out[3] = {k, v, r};
+    ProfScope ps(PH_GEMM, as_stream(stream), 3.0 * 2.0 * M * (double)N * K);
     return launch_gemm_kvr(dtype, A, lda, as, W, ldw, ws, M, N, K, out, ldo, as_stream(stream),
                            tile_n);
 }

@@ -113,24 +113,71 @@ def det_softmax_cdf(logits: torch.Tensor, cdf_T: int) -> torch.Tensor:
     return out
 
 
-def det_matmul(x: torch.Tensor, W: torch.Tensor, out_dtype=None) -> torch.Tensor:
-    """x f16 [M, K] @ W f16 [K, N] (reference [in, out] layout) with the
-    M-invariant krunch_b200 GEMM; fp32 accumulation."""
-    _chk(x, "x", (torch.float16,)), _chk(W, "W", (torch.float16,))
+def _det_matmul(x: torch.Tensor, W: torch.Tensor, out_dtype, kind: int, dt) -> torch.Tensor:
+    _chk(x, "x", (dt,)), _chk(W, "W", (dt,))
     M, K = x.shape
     K2, Nn = W.shape
     if K != K2:
         raise RuntimeError("inner dimensions differ")
     Kp, Np = (K + 63) // 64 * 64, (Nn + 127) // 128 * 128
-    Wt = torch.zeros((Np, Kp), dtype=torch.float16, device=W.device)
+    Wt = torch.zeros((Np, Kp), dtype=dt, device=W.device)
     Wt[:Nn, :K] = W.t()
     xa = x if Kp == K else torch.nn.functional.pad(x, (0, Kp - K)).contiguous()
     f32 = out_dtype == torch.float32
     out = torch.empty((M, Np), dtype=torch.float32 if f32 else torch.float16, device=x.device)
-    N.call("kb_gemm", N.KB_F16, xa.data_ptr(), Kp, Wt.data_ptr(), Kp, M, Np, Kp,
+    N.call("kb_gemm", kind, xa.data_ptr(), Kp, Wt.data_ptr(), Kp, M, Np, Kp,
            N.KB_EPI_F32 if f32 else N.KB_EPI_F16, out.data_ptr(), Np, None, None,
            N.stream_ptr(x.device))
-    return out[:, :Nn] if Np != Nn else out
+    out = out[:, :Nn] if Np != Nn else out
+    if out_dtype is not None and out.dtype != out_dtype:
+        out = out.to(out_dtype)
+    return out
+
+
+def det_matmul(x: torch.Tensor, W: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """x f16 [M, K] @ W f16 [K, N] (reference [in, out] layout) with the
+    M-invariant krunch_b200 GEMM; fp32 accumulation (layer_cpp.cpp:846-849)."""
+    return _det_matmul(x, W, out_dtype, N.KB_F16, torch.float16)
+
+
+def det_matmul_bf16(x: torch.Tensor, W: torch.Tensor, out_dtype=None) -> torch.Tensor:
+    """bf16 x [M, K] @ bf16 W [K, N], fp32 accumulation; bf16 out unless
+    out_dtype says otherwise (layer_cpp.cpp:850-870)."""
+    # bf16 output (the reference's default: x's dtype) rounds once from fp32
+    if out_dtype in (None, torch.bfloat16):
+        return _det_matmul(x, W, torch.float32, N.KB_BF16, torch.bfloat16).to(torch.bfloat16)
+    return _det_matmul(x, W, out_dtype, N.KB_BF16, torch.bfloat16)
+
+
+def det_matmul_tc_3way_async(A0, A1, A2, B0, B1, B2, out_dtype=None):
+    """(A0 @ B0, A1 @ B1, A2 @ B2) for inputs sharing [M, K] and weights
+    sharing [K, N] (layer_cpp.cpp:926-960): plain products in one dtype, as
+    the reference's binding returns them."""
+    for a in (A1, A2):
+        if a.shape != A0.shape:
+            raise RuntimeError("M must match")
+    for b in (B1, B2):
+        if b.shape[-1] != B0.shape[-1]:
+            raise RuntimeError("N must match")
+    return tuple(det_matmul(a, b, out_dtype) for a, b in zip((A0, A1, A2), (B0, B1, B2)))
+
+
+def reset_phase_times() -> None:
+    """Start accumulating per-phase device times (the reference's
+    KRUNCH_PHASE_PROFILE accumulators, layer_cpp.cpp:833-837): every library
+    launch until read_phase_times() is bracketed by CUDA events."""
+    N.profile_begin()
+
+
+def read_phase_times() -> dict:
+    """Milliseconds per phase since reset_phase_times(), plus call_count (the
+    launches counted); the phases are this library's (embed, ln_mix, gemm,
+    wkv, head, cdf, encode, decode, step).  Like the reference's, meant for
+    a single host thread; reading ends the accumulation."""
+    prof = N.profile_end()
+    d = {k: v[0] for k, v in prof.items()}
+    d["call_count"] = int(sum(v[1] for v in prof.values()))
+    return d
 
 
 # --------------------------------------------------------------------------

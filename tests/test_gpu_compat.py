@@ -217,3 +217,24 @@ def test_layer_step_cache_sees_in_place_edits(torch):
     assert len(krunch_ac_cuda._LAYER_CACHE) == 2 and not torch.equal(a, c)
     krunch_ac_cuda.clear_layer_graph_cache()
     assert torch.equal(run(), c)
+
+
+def test_reference_bench_names(torch):
+    """det_matmul_bf16 / det_matmul_tc_3way_async / phase-time readers under
+    the reference's names (layer_cpp.cpp:825-960) against torch fp32."""
+    import krunch_ac_cuda
+    g = torch.Generator(device="cuda").manual_seed(4)
+    x = (torch.randn((70, 768), device="cuda", generator=g) * 0.5)
+    W = (torch.randn((768, 300), device="cuda", generator=g) * 0.05)
+    ref = x @ W
+    yb = krunch_ac_cuda.det_matmul_bf16(x.bfloat16(), W.bfloat16())
+    assert yb.dtype == torch.bfloat16 and yb.shape == (70, 300)
+    refb = x.bfloat16().float() @ W.bfloat16().float()
+    assert (yb.float() - refb).abs().max().item() <= 2e-2 * max(1.0, refb.abs().max().item())
+    krunch_ac_cuda.reset_phase_times()
+    ys = krunch_ac_cuda.det_matmul_tc_3way_async(x.half(), x.half(), x.half(), W.half(),
+                                                 W.half(), W.half(), torch.float32)
+    times = krunch_ac_cuda.read_phase_times()
+    assert len(ys) == 3 and all(torch.equal(ys[0], y) for y in ys) and ys[0].dtype == torch.float32
+    assert (ys[0] - ref).abs().max().item() <= 2e-2
+    assert times["call_count"] == 3 and times["gemm"] > 0
