@@ -42,3 +42,6 @@ def test_host_only_calls():
     d.n_layer = 0
     assert lib.kb_model_create(ctypes.byref(d), ctypes.byref(h)) == -1
     assert lib.kb_forward_workspace_bytes(None, 1, 1) == 0
+    assert lib.kb_layer_forward(None, 0, None, 1, 1, None, None, 0, None) == -1
+    assert lib.kb_gemm_kvr(0, None, None, None, 768, None, None, None, None, None, None, 768,
+                           None, None, None, 1, 768, 768, None, None, None, 768, 0, None) == -1
