@@ -163,25 +163,29 @@ def test_large_window_odd_streams_with_state(torch, wdtype):
     assert torch.equal(st, st_big)
 
 
-@pytest.mark.parametrize("wdtype", ["f16", "i8"])
-def test_wide_rows_vs_oracle_and_stepped(torch, wdtype):
-    """C = 2048 (the 1.5B width) runs LayerNorm+mix in the streaming kernel:
-    logits near the oracle, packed == stepped bit for bit."""
+@pytest.mark.parametrize("wdtype,B,T", [("f16", 2, 6), ("i8", 2, 6), ("bf16", 2, 6),
+                                         ("f16", 3, 19), ("bf16", 3, 19)])
+def test_wide_rows_vs_oracle_and_stepped(torch, wdtype, B, T):
+    """C = 2048 (the 1.5B width) runs LayerNorm+mix in the streaming kernel
+    (fp16, bf16 and w8a8 outputs; ragged B x T): logits near the oracle,
+    packed == stepped bit for bit."""
     from krunch_b200.model import RWKVModel
     from oracle import rwkv
     w = random_weights(2, 2048, 8192, 300, seed=9)
     m = RWKVModel(w, wdtype=wdtype)
-    tok = np.random.default_rng(5).integers(0, 300, (2, 6))
+    tok = np.random.default_rng(5).integers(0, 300, (B, T))
     packed, st_p = _run(torch, m, tok)
-    ref, _ = rwkv.forward(w, tok, wdtype="i8" if wdtype == "i8" else "f32")
+    ref, _ = rwkv.forward(w, tok, wdtype=wdtype if wdtype != "f16" else "f32")
     d = np.abs(packed - ref)
-    if wdtype == "f16":
+    if wdtype == "bf16":
+        assert d.max() <= 5e-2
+    elif wdtype == "f16":
         assert d.max() <= LOGIT_TOL
     else:
         assert d.mean() <= 2e-2 and d.max() <= 0.15
-    st = m.new_state(2)
+    st = m.new_state(B)
     steps = []
-    for t in range(6):
+    for t in range(T):
         lg, st = _run(torch, m, tok[:, t:t + 1], st)
         steps.append(lg[:, 0])
     assert np.array_equal(np.stack(steps, 1), packed)
