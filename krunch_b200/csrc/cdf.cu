@@ -33,6 +33,8 @@
 #include <float.h>
 #include <limits.h>
 
+#include <atomic>
+
 #include "coder.cuh"
 #include "profile.cuh"
 #include "softmax_stats.cuh"
@@ -348,7 +350,11 @@ __device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int
         int c[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ls = 0;
         if (i0 < we) {
             float e[8];
-            if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
+            if (gs[i0 / SUBTILE] < 1.0f) {  // cold subtile: every count is 1 (see cdf_row_body)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) c[k] = i0 + k < we ? 1 : 0;
+                ls = min(8, we - i0);
+            } else if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
                 src.load8_full(i0, e);
                 ls = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
                            : counts8_full<false>(e, gs[i0 / SUBTILE], c);
@@ -394,6 +400,22 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
     for (int base = wa; base < we; base += 256) {
         const int i0 = base + lane * 8;
         if (i0 >= we) continue;
+        if (gs[i0 / SUBTILE] < 1.0f) {
+            // cold subtile: e_i <= 1 (numerators are relative to the
+            // subtile's max), so q_i = fl(e_i * gs_u) <= gs_u < 1 and every
+            // count is floor(q_i) + 1 = 1 -- the numerators are not read
+            const int n = min(8, we - i0);
+            cs += n;
+            if (MODE == MODE_LOHI) {
+                if (i0 + n <= sym) {
+                    below += n;
+                } else if (i0 <= sym) {
+                    below += sym - i0;
+                    rs.csym = 1;
+                }
+            }
+            continue;
+        }
         float e[8];
         int c[8];
         int step;
@@ -577,6 +599,192 @@ __global__ void __launch_bounds__(CDF_NT) k_cdf(const uint16_t* __restrict__ log
     }
 }
 
+// ---------------------------------------------------------------------------
+// (lo, hi) of the row's symbol with one warp per row (the compress hot path:
+// numerators and partials from the head GEMM, 16-byte aligned rows).  Same
+// numbers as k_cdf<MODE_LOHI>, computed without a CTA barrier so that the
+// SM holds 48-64 rows at once and one row's reduction latency hides behind
+// the others' loads:
+// * the normaliser follows the 512-virtual-thread order of row_setup:
+//   virtual thread 32j + lane folds u = 32j + lane + 512k in order, each
+//   virtual warp j reduces by the xor butterfly, and the 16 warp partials
+//   (identity-padded to 32 lanes) meet in the same butterfly;
+// * lane l takes whole subtiles u = l + 32k (64 contiguous bytes, four
+//   16-byte loads), with gs_u computed once per subtile;
+// * the argmax is the (gs_u desc, u asc) maximum, then the first e == 1 in it.
+// ---------------------------------------------------------------------------
+#ifndef KB_CDF_WARP
+#define KB_CDF_WARP 1
+#endif
+constexpr int CW_WARPS = 8;
+#ifndef KB_CDFW_NJ
+#define KB_CDFW_NJ 8  // virtual warps whose partials are folded together
+#endif
+
+__global__ void __launch_bounds__(CW_WARPS * 32)
+    k_cdf_lohi_warp(const uint16_t* __restrict__ logits, int64_t stride, int V, int bits,
+                    const float2* __restrict__ stats, int64_t stats_stride,
+                    const int32_t* __restrict__ symbols, uint2* __restrict__ out, int rows) {
+    extern __shared__ float cw_m[];  // per warp: the subtile maxima m_u of its row
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * CW_WARPS + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const uint16_t* x = logits + (int64_t)row * stride;
+    const float2* p = stats + (int64_t)row * stats_stride;
+    const int nsub = (V + SUBTILE - 1) / SUBTILE;
+    float* ms = cw_m + (threadIdx.x >> 5) * nsub;
+    const int T = 1 << bits;
+    const float scale = (float)(T - V);
+    const bool small = (T - V) < (1 << 23);
+    int sym = symbols[row];
+    sym = sym < 0 ? 0 : (sym >= V ? V - 1 : sym);
+
+    // ---- normaliser (M, 1/S) ---------------------------------------------
+    // virtual warps in batches of NJ: the loads of a batch are issued
+    // together and its butterflies interleave
+    MS w{-INFINITY, 0.0f};
+    constexpr int NJ = KB_CDFW_NJ;
+    for (int j0 = 0; j0 < CDF_NW; j0 += NJ) {
+        MS acc[NJ];
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) acc[j] = MS{-INFINITY, 0.0f};
+        for (int u0 = 32 * j0 + lane; u0 < nsub; u0 += CDF_NT) {
+            float2 q[NJ];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                q[j] = u0 + 32 * j < nsub ? p[u0 + 32 * j] : make_float2(0.0f, 0.0f);
+#pragma unroll
+            for (int j = 0; j < NJ; ++j)
+                if (u0 + 32 * j < nsub) {
+                    acc[j] = ms_merge(acc[j], MS{q[j].x, q[j].y});
+                    ms[u0 + 32 * j] = q[j].x;
+                }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) acc[j] = ms_merge(acc[j], ms_shfl_xor(acc[j], off));
+        }
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            if (lane == j0 + j) w = acc[j];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) w = ms_merge(w, ms_shfl_xor(w, off));
+    const float M = w.m, inv = __frcp_rn(w.s);
+
+    // ---- counts -------------------------------------------------------------
+    // Step k: lane l owns subtile u = 32k + l and its factor gs_u.  A cold
+    // subtile (gs_u < 1: e_i <= 1, so q_i = fl(e_i * gs_u) <= gs_u < 1) has
+    // every count 1 and its numerators are not read.  The hot ones are
+    // counted by the whole warp, eight at a time: lanes 4q..4q+3 take 8
+    // elements each of the q-th hot subtile (one 16-byte load per lane).
+    __shared__ int cw_sidx[CW_WARPS][8];
+    int* sidx = cw_sidx[threadIdx.x >> 5];
+    const unsigned lt = (1u << lane) - 1u;
+    const int usym = sym / SUBTILE;
+    float best = -INFINITY, gsym = 0.0f;
+    int bu = INT_MAX, cs = 0, below = 0;
+    for (int k0 = 0; k0 < nsub; k0 += 32) {
+        const int u = k0 + lane;
+        const bool valid = u < nsub;
+        const int i0 = u * SUBTILE;
+        const int n = valid ? min(SUBTILE, V - i0) : 0;
+        const float g =
+            valid ? __fmul_rn(__fmul_rn(kb_expf(__fsub_rn(ms[u], M)), inv), scale) : 0.0f;
+        if (valid && g > best) {
+            best = g;
+            bu = u;
+        }
+        if (u == usym) gsym = g;
+        const bool hot = valid && g >= 1.0f && n == SUBTILE;
+        int csub = 0;
+        if (valid && !hot) {
+            if (g < 1.0f) {
+                csub = n;
+            } else {  // the row's last, partial subtile
+                for (int j = 0; j < n; ++j) csub += (int)floorf(__fmul_rn(h2f(x[i0 + j]), g)) + 1;
+            }
+        }
+        unsigned rem = __ballot_sync(0xffffffffu, hot);
+        while (rem) {
+            const int r = __popc(rem & lt);
+            const bool mine = ((rem >> lane) & 1u) && r < 8;
+            if (mine) sidx[r] = lane;
+            __syncwarp();
+            const int nh = min(8, __popc(rem));
+            const int q = lane >> 2;
+            const int sl = sidx[q < nh ? q : 0];
+            const float gq = __shfl_sync(0xffffffffu, g, sl);
+            int part = 0;
+            if (q < nh) {
+                float e[8];
+                int c[8];
+                unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)(k0 + sl) * SUBTILE +
+                                                        8 * (lane & 3)),
+                        e);
+                part = small ? counts8_full<true>(e, gq, c) : counts8_full<false>(e, gq, c);
+            }
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            const int got = __shfl_sync(0xffffffffu, part, 4 * (r & 7));
+            if (mine) csub = got;
+            rem &= ~__ballot_sync(0xffffffffu, mine);
+            __syncwarp();
+        }
+        cs += csub;
+        if (u < usym) below += csub;
+    }
+    // the symbol's own subtile, one element per lane
+    int csym;
+    {
+        const float g = __shfl_sync(0xffffffffu, gsym, usym & 31);
+        const int i = usym * SUBTILE + lane;
+        int c = 0;
+        if (i < V) c = g < 1.0f ? 1 : (int)floorf(__fmul_rn(h2f(x[i]), g)) + 1;
+        csym = __shfl_sync(0xffffffffu, c, sym & 31);
+        below += i < sym ? c : 0;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        cs += __shfl_xor_sync(0xffffffffu, cs, off);
+        below += __shfl_xor_sync(0xffffffffu, below, off);
+        am_merge(best, bu, __shfl_xor_sync(0xffffffffu, best, off),
+                 __shfl_xor_sync(0xffffffffu, bu, off));
+    }
+    const int a = bu * SUBTILE;
+    const unsigned b0 = __ballot_sync(0xffffffffu, a + lane < V && x[a + lane] == (uint16_t)0x3C00u);
+    const int amax = a + __ffs(b0) - 1;
+    if (lane == 0) {
+        const int deficit = T - cs;
+        const uint32_t lo = (uint32_t)(below + (amax < sym ? deficit : 0));
+        const uint32_t hi = lo + (uint32_t)(csym + (amax == sym ? deficit : 0));
+        out[row] = make_uint2(lo, hi);
+    }
+}
+
+static int launch_cdf_lohi_warp(int rows, const uint16_t* logits, int64_t stride, int V, int bits,
+                                const float* stats, int64_t stats_stride, const int32_t* symbols,
+                                void* out, cudaStream_t st) {
+    ProfScope ps(PH_CDF, st, (double)rows * ((double)V * 2 + 16.0));
+    const int grid = (rows + CW_WARPS - 1) / CW_WARPS;
+    const size_t smem = (size_t)CW_WARPS * ((V + SUBTILE - 1) / SUBTILE) * sizeof(float);
+    static std::atomic<unsigned long long> done{0};
+    const cudaError_t e = once_per_device(done, [] {
+        return cudaFuncSetAttribute(k_cdf_lohi_warp, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)(CW_WARPS * MAX_SUB * sizeof(float)));
+    });
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return KB_ERR_CUDA;
+    }
+    k_cdf_lohi_warp<<<grid, CW_WARPS * 32, smem, st>>>(logits, stride, V, bits,
+                                                     reinterpret_cast<const float2*>(stats),
+                                                     stats_stride, symbols,
+                                                     reinterpret_cast<uint2*>(out), rows);
+    return launch_status();
+}
+
 struct CdfArgs {
     const uint16_t* logits;
     int64_t stride;
@@ -637,6 +845,9 @@ extern "C" int kb_cdf_rows(const uint16_t* logits, int64_t row_stride, int rows,
         case KB_CDF_LOHI: {
             if (!symbols) return KB_ERR_ARG;
             if ((reinterpret_cast<uintptr_t>(out) & 7u) != 0) return KB_ERR_ALIGN;
+            if (KB_CDF_WARP && logit_stats && aligned16(logits) && row_stride % 8 == 0)
+                return launch_cdf_lohi_warp(rows, logits, row_stride, V, bits, logit_stats,
+                                            stats_stride, symbols, out, st);
             return launch_cdf<MODE_LOHI>(rows, a, st);
         }
         default:

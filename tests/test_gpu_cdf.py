@@ -151,3 +151,40 @@ def test_head_gemm_numerators_match_oracle(torch):
         outs.append(o.cpu().numpy())
     assert np.array_equal(outs[0], outs[1])
     assert np.array_equal(outs[0].view(np.uint32), coder.lohi_from_logits(raw_h, sym.cpu().numpy(), 16))
+
+
+@pytest.mark.parametrize("bits", [16, 24])
+@pytest.mark.parametrize("V,stride", [(50277, 50304), (1000, 1000), (40, 48), (1001, 1001)])
+def test_lohi_from_head_parts_vs_oracle(torch, V, stride, bits):
+    """(lo, hi) from stored numerators + partials (the compress path: one warp
+    per row, cold subtiles not read) == the oracle's, on flat, peaked,
+    all-equal and scaled rows, with symbols at 0, V - 1, the argmax, inside
+    and at the edges of subtiles."""
+    from krunch_b200 import _native as N
+    rng = np.random.default_rng(V + bits)
+    x = random_logits(12, V, seed=V * 7 + bits)
+    x[0] = 0
+    x[1, V // 2] = 30
+    x[2] *= 8.0          # peaked: most subtiles cold
+    x[3] *= 0.05         # near-flat: every subtile cold at 16 bits
+    x[4, :] = -5.0
+    x[4, 37 % V] = 4.0
+    x = x.astype(np.float16).astype(np.float32)
+    e16, ms = coder.softmax_parts(x)
+    nsub = ms.shape[1]
+    num = np.zeros((12, stride), np.float16)
+    num[:, :V] = e16[:, :V]   # (1001: unaligned rows take the one-CTA-per-row kernel)
+    st_stride = nsub + (nsub & 1)
+    stats = np.zeros((12, st_stride, 2), np.float32)
+    stats[:, :nsub] = ms
+    sym = rng.integers(0, V, 12)
+    sym[:5] = [0, V // 2, int(np.argmax(x[2])), V - 1, 37 % V]
+    sym[5] = 31 % V
+    sym[6] = 32 % V
+    xd = torch.from_numpy(num).cuda()
+    sd = torch.from_numpy(stats).cuda()
+    yd = torch.from_numpy(sym.astype(np.int32)).cuda()
+    o = torch.empty((12, 2), dtype=torch.int32, device="cuda")
+    N.call("kb_cdf_rows", xd.data_ptr(), stride, 12, V, bits, N.KB_CDF_LOHI, sd.data_ptr(),
+           st_stride, yd.data_ptr(), o.data_ptr(), N.stream_ptr())
+    assert np.array_equal(o.cpu().numpy().view(np.uint32), coder.lohi_from_logits(x, sym, bits))
