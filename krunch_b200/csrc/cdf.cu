@@ -620,6 +620,9 @@ constexpr int CW_WARPS = 8;
 #ifndef KB_CDFW_NJ
 #define KB_CDFW_NJ 8  // virtual warps whose partials are folded together
 #endif
+#ifndef KB_CDFW_RU
+#define KB_CDFW_RU 4  // rounds of hot-subtile loads in flight
+#endif
 
 __global__ void __launch_bounds__(CW_WARPS * 32)
     k_cdf_lohi_warp(const uint16_t* __restrict__ logits, int64_t stride, int V, int bits,
@@ -674,17 +677,17 @@ __global__ void __launch_bounds__(CW_WARPS * 32)
     const float M = w.m, inv = __frcp_rn(w.s);
 
     // ---- counts -------------------------------------------------------------
-    // Step k: lane l owns subtile u = 32k + l and its factor gs_u.  A cold
-    // subtile (gs_u < 1: e_i <= 1, so q_i = fl(e_i * gs_u) <= gs_u < 1) has
-    // every count 1 and its numerators are not read.  The hot ones are
-    // counted by the whole warp, eight at a time: lanes 4q..4q+3 take 8
-    // elements each of the q-th hot subtile (one 16-byte load per lane).
-    __shared__ int cw_sidx[CW_WARPS][8];
-    int* sidx = cw_sidx[threadIdx.x >> 5];
+    // Pass 1, step k: lane l owns subtile u = 32k + l and its factor gs_u.  A
+    // cold subtile (gs_u < 1: e_i <= 1, so q_i = fl(e_i * gs_u) <= gs_u < 1)
+    // has every count 1 and its numerators are not read; a hot one is
+    // appended to a list kept in the already-consumed front of ms[].
+    // Pass 2 counts the hot subtiles with the whole warp: lanes 4q..4q+3
+    // take 8 elements each of list entry 8r + q, RU rounds of loads in flight.
     const unsigned lt = (1u << lane) - 1u;
+    int* hot_u = reinterpret_cast<int*>(ms);
     const int usym = sym / SUBTILE;
     float best = -INFINITY, gsym = 0.0f;
-    int bu = INT_MAX, cs = 0, below = 0;
+    int bu = INT_MAX, cs = 0, below = 0, nhot = 0;
     for (int k0 = 0; k0 < nsub; k0 += 32) {
         const int u = k0 + lane;
         const bool valid = u < nsub;
@@ -706,34 +709,44 @@ __global__ void __launch_bounds__(CW_WARPS * 32)
                 for (int j = 0; j < n; ++j) csub += (int)floorf(__fmul_rn(h2f(x[i0 + j]), g)) + 1;
             }
         }
-        unsigned rem = __ballot_sync(0xffffffffu, hot);
-        while (rem) {
-            const int r = __popc(rem & lt);
-            const bool mine = ((rem >> lane) & 1u) && r < 8;
-            if (mine) sidx[r] = lane;
-            __syncwarp();
-            const int nh = min(8, __popc(rem));
-            const int q = lane >> 2;
-            const int sl = sidx[q < nh ? q : 0];
-            const float gq = __shfl_sync(0xffffffffu, g, sl);
+        cs += csub;
+        if (u < usym) below += csub;
+        const unsigned hm = __ballot_sync(0xffffffffu, hot);
+        if (hot) hot_u[nhot + __popc(hm & lt)] = u;  // index <= u: already read
+        nhot += __popc(hm);
+    }
+    __syncwarp();
+    constexpr int RU = KB_CDFW_RU;
+    const int q = lane >> 2;
+    for (int j0 = 0; j0 < nhot; j0 += 8 * RU) {
+        uint4 v[RU];
+        int uu[RU];
+#pragma unroll
+        for (int r = 0; r < RU; ++r) {
+            const int j = j0 + 8 * r + q;
+            uu[r] = j < nhot ? hot_u[j] : -1;
+            v[r] = uu[r] >= 0 ? *reinterpret_cast<const uint4*>(x + (int64_t)uu[r] * SUBTILE +
+                                                                 8 * (lane & 3))
+                              : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int r = 0; r < RU; ++r) {
             int part = 0;
-            if (q < nh) {
+            if (uu[r] >= 0) {
+                const float g =
+                    __fmul_rn(__fmul_rn(kb_expf(__fsub_rn(p[uu[r]].x, M)), inv), scale);
                 float e[8];
                 int c[8];
-                unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)(k0 + sl) * SUBTILE +
-                                                        8 * (lane & 3)),
-                        e);
-                part = small ? counts8_full<true>(e, gq, c) : counts8_full<false>(e, gq, c);
+                unpack8(v[r], e);
+                part = small ? counts8_full<true>(e, g, c) : counts8_full<false>(e, g, c);
             }
             part += __shfl_xor_sync(0xffffffffu, part, 1);
             part += __shfl_xor_sync(0xffffffffu, part, 2);
-            const int got = __shfl_sync(0xffffffffu, part, 4 * (r & 7));
-            if (mine) csub = got;
-            rem &= ~__ballot_sync(0xffffffffu, mine);
-            __syncwarp();
+            if ((lane & 3) == 0 && uu[r] >= 0) {
+                cs += part;
+                if (uu[r] < usym) below += part;
+            }
         }
-        cs += csub;
-        if (u < usym) below += csub;
     }
     // the symbol's own subtile, one element per lane
     int csym;
