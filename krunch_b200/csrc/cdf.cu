@@ -646,7 +646,7 @@ __global__ void __launch_bounds__(CW_WARPS * 32)
     // virtual warps in batches of NJ: the loads of a batch are issued
     // together and its butterflies interleave
     MS w{-INFINITY, 0.0f};
-    constexpr int NJ = KB_CDFW_NJ;
+    constexpr int NJ = KB_CDFW_NJ;  // a power of two, at most 16
     for (int j0 = 0; j0 < CDF_NW; j0 += NJ) {
         MS acc[NJ];
 #pragma unroll
@@ -663,14 +663,30 @@ __global__ void __launch_bounds__(CW_WARPS * 32)
                     ms[u0 + 32 * j] = q[j].x;
                 }
         }
+        // The xor butterflies of the NJ virtual warps by recursive halving:
+        // at offset `off` a lane keeps the half of its values selected by
+        // lane bit `off` and merges it with the partner's copy of that half.
+        // The partner shares every bit used so far, so it holds the same
+        // partials the plain butterfly would, and ms_merge is symmetric: the
+        // results are the butterflies' bits.  Lanes 32/NJ*j.. hold warp j0+j.
+        constexpr int LV = NJ >= 16 ? 4 : NJ >= 8 ? 3 : NJ >= 4 ? 2 : NJ >= 2 ? 1 : 0;
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
+        for (int lv = 0; lv < LV; ++lv) {
+            const int h = (NJ >> lv) / 2, off = 16 >> lv;
+            const bool up = (lane & off) != 0;
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) acc[j] = ms_merge(acc[j], ms_shfl_xor(acc[j], off));
+            for (int i = 0; i < h; ++i) {
+                const MS keep = up ? acc[h + i] : acc[i];
+                const MS give = up ? acc[i] : acc[h + i];
+                acc[i] = ms_merge(keep, ms_shfl_xor(give, off));
+            }
         }
 #pragma unroll
-        for (int j = 0; j < NJ; ++j)
-            if (lane == j0 + j) w = acc[j];
+        for (int off = 16 >> LV; off > 0; off >>= 1)
+            acc[0] = ms_merge(acc[0], ms_shfl_xor(acc[0], off));
+        const MS wj = MS{__shfl_sync(0xffffffffu, acc[0].m, (32 / NJ) * ((lane - j0) & (NJ - 1))),
+                         __shfl_sync(0xffffffffu, acc[0].s, (32 / NJ) * ((lane - j0) & (NJ - 1)))};
+        if (lane >= j0 && lane < j0 + NJ) w = wj;
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) w = ms_merge(w, ms_shfl_xor(w, off));
