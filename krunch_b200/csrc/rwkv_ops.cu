@@ -580,13 +580,16 @@ int launch_quant_rows(const uint16_t* x, int R, int K, int8_t* q, float* scale, 
 // LayerNorm + token-shift mix over tiles of consecutive rows (fp16 / bf16
 // outputs, C = 32 EPL <= 1024).  A tile's rows are contiguous in memory, so
 // one 1-D bulk copy brings them (and the row before the tile) into shared
-// memory; a persistent CTA double-buffers its tiles on an mbarrier, so the
-// next tile streams in while this one is computed.  Phase 1: each warp takes
-// row pairs and computes their LayerNorm exactly as ln_warp_h2x2 does (same
-// lane order and butterfly), writing the fp16
-// result back in place; warp 0 also normalises the row before the tile when
-// the tile's first row takes its token-shift input from it.  Phase 2: the
-// mixes, one 16-byte chunk per thread at a time, coalesced across the CTA.
+// memory; a persistent CTA (as many per SM as registers and shared memory
+// allow, the grid sized by the occupancy query) walks a contiguous run of
+// tiles and double-buffers them on an mbarrier, so the next tile streams in
+// while this one is computed.  Phase 1: each warp takes row pairs and
+// computes their LayerNorm exactly as ln_warp_h2x2 does (same lane order and
+// butterfly), writing the fp16 result back in place.  The row before a tile
+// (the token-shift input of its first row) is the previous tile's last row,
+// whose LayerNorm the CTA keeps from that tile; only a run's first tile
+// normalises it again.  Phase 2: the mixes, one 16-byte chunk per thread at
+// a time, coalesced across the CTA.
 // ---------------------------------------------------------------------------
 #ifndef KB_LNT_RT
 #define KB_LNT_RT 16
@@ -603,11 +606,14 @@ struct LnTile {
     static constexpr int RT = EPL <= 24 ? KB_LNT_RT : KB_LNT_RT / 2;  // rows per tile
     static constexpr uint32_t ROW = (uint32_t)C * 2;     // bytes per fp16 row
     static constexpr uint32_t BUF = (RT + 1) * ROW;      // slot 0: the row before
-    static constexpr size_t SMEM = 2 * BUF + 64 + 128;   // two buffers + barriers + align
+    // two buffers + the carried row + barriers + align
+    static constexpr size_t SMEM = 2 * BUF + ROW + 64 + 128;
+    // resident CTAs per SM the register budget is sized for
+    static constexpr int MINB = EPL <= 24 ? 3 : 2;
 };
 
 template <int NMIX, int EPL>
-__global__ void __launch_bounds__(LNT_WARPS * 32)
+__global__ void __launch_bounds__(LNT_WARPS * 32, LnTile<EPL>::MINB)
     k_ln_mix_tile(const uint16_t* __restrict__ x, int B, int T, const float* __restrict__ lw,
                   const float* __restrict__ lb, MixArgs ma, const float* __restrict__ state_in,
                   float* __restrict__ state_out, uint16_t* __restrict__ xx_out) {
@@ -615,11 +621,16 @@ __global__ void __launch_bounds__(LNT_WARPS * 32)
     constexpr int C = L::C, RT = L::RT, H = EPL / 2, CH = C / 8;
     extern __shared__ unsigned char lnt_raw[];
     unsigned char* smem = lnt_raw + ((128u - (tc::smem_addr(lnt_raw) & 127u)) & 127u);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * L::BUF);
+    unsigned char* carry = smem + 2 * L::BUF;  // LN of the last row of this CTA's previous tile
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * L::BUF + L::ROW);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rows = (int64_t)B * T;
     const int64_t tiles = (rows + RT - 1) / RT;
-    if ((int64_t)blockIdx.x >= tiles) return;
+    // a contiguous run of tiles per CTA: the row before a tile is the last
+    // row of the tile before it, already normalised by this CTA
+    const int64_t t_begin = (int64_t)blockIdx.x * tiles / gridDim.x;
+    const int64_t t_end = (int64_t)(blockIdx.x + 1) * tiles / gridDim.x;
+    if (t_begin >= t_end) return;
     // rows [r0 - 1, r0 + n) of tile `tile` into buffer `bi` (slot 0 = r0 - 1)
     auto issue = [&](int64_t tile, int bi) {
         const int64_t r0 = tile * RT;
@@ -634,22 +645,23 @@ __global__ void __launch_bounds__(LNT_WARPS * 32)
         tc::mbar_init(&full[0], 1);
         tc::mbar_init(&full[1], 1);
         tc::fence_barrier_init();
-        issue(blockIdx.x, 0);
+        issue(t_begin, 0);
     }
     __syncthreads();
     int it = 0;
-    for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+    bool carried = false;  // `carry` holds the LN of row r0 - 1 of this tile
+    for (int64_t tile = t_begin; tile < t_end; ++tile, ++it) {
         const int bi = it & 1;
-        if (threadIdx.x == 0 && tile + gridDim.x < tiles) {
+        if (threadIdx.x == 0 && tile + 1 < t_end) {
             tc::fence_proxy_async_smem();  // this buffer's generic accesses (two tiles ago)
-            issue(tile + gridDim.x, bi ^ 1);
+            issue(tile + 1, bi ^ 1);
         }
         if (!tc::mbar_wait(&full[bi], (uint32_t)(it >> 1) & 1u)) {
             // bounded wait expired: report, let the other buffer's copy (if
             // any) land, and leave
             if (threadIdx.x == 0) {
                 atomicExch(&g_ln_error, 1);
-                if (tile + gridDim.x < tiles) tc::mbar_wait(&full[bi ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
+                if (tile + 1 < t_end) tc::mbar_wait(&full[bi ^ 1], (uint32_t)((it + 1) >> 1) & 1u);
             }
             return;
         }
@@ -681,7 +693,11 @@ __global__ void __launch_bounds__(LNT_WARPS * 32)
                         make_uint4(ob[4 * j], ob[4 * j + 1], ob[4 * j + 2], ob[4 * j + 3]);
             }
         }
-        if (need_prev && warp == (((n + 1) / 2) % LNT_WARPS)) {  // the least loaded warp
+        if (need_prev && carried) {
+            // slot 0 <- the carried row (bulk copy landed: plain writes now)
+            for (int c = threadIdx.x; c < CH; c += LNT_WARPS * 32)
+                reinterpret_cast<uint4*>(buf)[c] = reinterpret_cast<const uint4*>(carry)[c];
+        } else if (need_prev && warp == (((n + 1) / 2) % LNT_WARPS)) {  // the least loaded warp
             uint32_t* rp = reinterpret_cast<uint32_t*>(buf);
             uint32_t vp[H], op[H];
 #pragma unroll
@@ -697,10 +713,19 @@ __global__ void __launch_bounds__(LNT_WARPS * 32)
         }
         __syncthreads();
         // ---- phase 2: token-shift mixes, xx / state outputs --------------------
+        const int b0 = (int)(r0 / T), t0 = (int)(r0 - (int64_t)b0 * T);
+        if (n == RT && tile + 1 < t_end)  // the next tile's row before it
+            for (int c = threadIdx.x; c < CH; c += LNT_WARPS * 32)
+                reinterpret_cast<uint4*>(carry)[c] = reinterpret_cast<const uint4*>(buf + RT * L::ROW)[c];
+        carried = n == RT && tile + 1 < t_end;
         for (int q = threadIdx.x; q < n * CH; q += LNT_WARPS * 32) {
             const int r = q / CH, ch = q - r * CH;
             const int64_t g = r0 + r;
-            const int b = (int)(g / T), t = (int)(g - (int64_t)b * T);
+            int b = b0, t = t0 + r;
+            if (t >= T) {
+                b += t / T;
+                t %= T;
+            }
             const uint4 cq = reinterpret_cast<const uint4*>(buf + (1 + r) * L::ROW)[ch];
             const uint32_t cu[4] = {cq.x, cq.y, cq.z, cq.w};
             if (NMIX > 0) {
@@ -781,7 +806,18 @@ int launch_ln_tile(int B, int T, cudaStream_t st, const uint16_t* x, const float
     int sms = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int per_sm = (int)(220000 / L::SMEM) > 0 ? (int)(220000 / L::SMEM) : 1;
+    // resident CTAs per SM (registers and shared memory), measured once
+    static std::atomic<int> occ[64];
+    int per_sm = dev >= 0 && dev < 64 ? occ[dev].load() : 0;
+    if (per_sm <= 0) {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_ln_mix_tile<NMIX, EPL>,
+                                                          LNT_WARPS * 32, L::SMEM) != cudaSuccess ||
+            per_sm <= 0) {
+            cudaGetLastError();
+            per_sm = 1;
+        }
+        if (dev >= 0 && dev < 64) occ[dev].store(per_sm);
+    }
     const int64_t cap = (int64_t)(sms > 0 ? sms : 148) * (per_sm < KB_LNT_CAP ? per_sm : KB_LNT_CAP);
     const int grid = (int)(tiles < cap ? tiles : cap);
     k_ln_mix_tile<NMIX, EPL><<<grid, LNT_WARPS * 32, L::SMEM, st>>>(x, B, T, lw, lb, ma, state_in,
