@@ -43,6 +43,8 @@ namespace kb {
 
 constexpr int CDF_NT = 512;
 constexpr int CDF_NW = CDF_NT / 32;
+// 256-element steps per warp range: V <= CDF_NW * 256 * CT_STEPS
+constexpr int CT_STEPS = 16;
 constexpr int MODE_COUNTS = KB_CDF_COUNTS;
 constexpr int MODE_CDF = KB_CDF_CDF;
 constexpr int MODE_LOHI = KB_CDF_LOHI;
@@ -337,6 +339,35 @@ __device__ __forceinline__ void raw_partials(const uint16_t* x, int V, int nsub,
     __syncthreads();
 }
 
+// Counts of the 8 elements from i0 (deficit added at the argmax), their sum.
+template <class Src>
+__device__ __forceinline__ int chunk_counts(const Src& src, const float* gs, int i0, int we,
+                                            int amax, int deficit, bool small, int (&c)[8]) {
+    int ls = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) c[k] = 0;
+    if (i0 < we) {
+        float e[8];
+        if (gs[i0 / SUBTILE] < 1.0f) {  // cold subtile: every count is 1 (see cdf_row_body)
+#pragma unroll
+            for (int k = 0; k < 8; ++k) c[k] = i0 + k < we ? 1 : 0;
+            ls = min(8, we - i0);
+        } else if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
+            src.load8_full(i0, e);
+            ls = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
+                       : counts8_full<false>(e, gs[i0 / SUBTILE], c);
+        } else {
+            src.load8(i0, we, e);
+            ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (i0 + k == amax) c[k] += deficit;
+        if (amax >= i0 && amax < i0 + 8) ls += deficit;
+    }
+    return ls;
+}
+
 // Walk the warp's range in 256-element steps: per step each lane's 8 counts
 // (deficit added at the argmax) and their warp-inclusive prefix.  f(i0, c,
 // ls, excl_in_warp_step, step_total) is called for every step; returning
@@ -347,26 +378,8 @@ __device__ __forceinline__ void walk_counts(const Src& src, const float* gs, int
     const int lane = threadIdx.x & 31;
     for (int base = wa; base < we; base += 256) {
         const int i0 = base + lane * 8;
-        int c[8] = {0, 0, 0, 0, 0, 0, 0, 0}, ls = 0;
-        if (i0 < we) {
-            float e[8];
-            if (gs[i0 / SUBTILE] < 1.0f) {  // cold subtile: every count is 1 (see cdf_row_body)
-#pragma unroll
-                for (int k = 0; k < 8; ++k) c[k] = i0 + k < we ? 1 : 0;
-                ls = min(8, we - i0);
-            } else if (i0 + 8 <= we && (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0) {
-                src.load8_full(i0, e);
-                ls = small ? counts8_full<true>(e, gs[i0 / SUBTILE], c)
-                           : counts8_full<false>(e, gs[i0 / SUBTILE], c);
-            } else {
-                src.load8(i0, we, e);
-                ls = counts8(e, gs[i0 / SUBTILE], i0, we, c);
-            }
-#pragma unroll
-            for (int k = 0; k < 8; ++k)
-                if (i0 + k == amax) c[k] += deficit;
-            if (amax >= i0 && amax < i0 + 8) ls += deficit;
-        }
+        int c[8];
+        const int ls = chunk_counts(src, gs, i0, we, amax, deficit, small, c);
         int inc = ls;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
@@ -386,6 +399,9 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
                              int64_t hist_stride) {
     __shared__ int s_wsum[CDF_NW], s_wexcl[CDF_NW], s_owner, s_sym;
     __shared__ uint32_t s_target, s_lo, s_hi;
+    // DECODE: count total of every 256-element step of each warp's range
+    // (deficit excluded), step k of warp w at s_ct[w][k]
+    __shared__ int s_ct[MODE == MODE_DECODE ? CDF_NW * CT_STEPS : 1];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = 1 << bits;
     const int Lw = ((V + CDF_NW * 256 - 1) / (CDF_NW * 256)) * 256;
@@ -397,8 +413,10 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
     const bool aligned_row = (reinterpret_cast<uintptr_t>(src.x) & 15u) == 0;
     const bool small = (T - V) < (1 << 23);
     int cs = 0, below = 0;
-    for (int base = wa; base < we; base += 256) {
+    for (int base = wa, ks = 0; base < we; base += 256, ++ks) {
         const int i0 = base + lane * 8;
+        const int cs0 = cs;
+        do {  // one chunk; `continue` leaves it
         if (i0 >= we) continue;
         if (gs[i0 / SUBTILE] < 1.0f) {
             // cold subtile: e_i <= 1 (numerators are relative to the
@@ -454,6 +472,14 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
                     if (i0 + k == sym) rs.csym = c[k];
                 }
             }
+        }
+        } while (0);
+        if (MODE == MODE_DECODE) {
+            // this step's count total over the warp, for the owner search
+            int v = cs - cs0;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) s_ct[warp * CT_STEPS + ks] = v;
         }
     }
     if (MODE == MODE_LOHI) {
@@ -513,28 +539,39 @@ __device__ void cdf_row_body(const Src& src, int V, int bits, const float* gs, R
         s_owner = tid;
     __syncthreads();
     if (warp == s_owner) {
-        int run = s_wexcl[warp];
-        walk_counts(src, gs, wa, we, amax, deficit, small,
-                    [&](int i0, const int (&c)[8], int ls, int excl, int total) {
-                        if (target >= (uint32_t)(run + total)) {
-                            run += total;
-                            return false;
-                        }
-                        int r = run + excl;
-                        if (ls > 0 && (uint32_t)r <= target && target < (uint32_t)(r + ls)) {
+        // the step totals recorded by the element pass locate the 256-element
+        // step holding the target; only that step's counts are recomputed
+        int run = s_wexcl[warp], base = wa;
+        for (int ks = 0; base < we; base += 256, ++ks) {
+            const int tot = s_ct[warp * CT_STEPS + ks] +
+                            ((amax >= base && amax < min(base + 256, we)) ? deficit : 0);
+            if (target < (uint32_t)(run + tot)) break;
+            run += tot;
+        }
+        if (base < we) {
+            const int i0 = base + lane * 8;
+            int c[8];
+            const int ls = chunk_counts(src, gs, i0, we, amax, deficit, small, c);
+            int inc = ls;
 #pragma unroll
-                            for (int k = 0; k < 8; ++k) {
-                                if (c[k] > 0 && target < (uint32_t)(r + c[k])) {
-                                    s_sym = i0 + k;
-                                    s_lo = (uint32_t)r;
-                                    s_hi = (uint32_t)(r + c[k]);
-                                    break;
-                                }
-                                r += c[k];
-                            }
-                        }
-                        return true;
-                    });
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inc, off);
+                if (lane >= off) inc += y;
+            }
+            int r = run + inc - ls;
+            if (ls > 0 && (uint32_t)r <= target && target < (uint32_t)(r + ls)) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (c[j] > 0 && target < (uint32_t)(r + c[j])) {
+                        s_sym = i0 + j;
+                        s_lo = (uint32_t)r;
+                        s_hi = (uint32_t)(r + c[j]);
+                        break;
+                    }
+                    r += c[j];
+                }
+            }
+        }
     }
     __syncthreads();
     if (tid == 0) {
