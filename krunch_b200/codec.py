@@ -237,7 +237,9 @@ class CompressPlan:
         """Kernels of this library that run() launches."""
         m = self.codec.model
         L = m.spec.n_layer
-        per_layer = 12 if m.spec.wdtype == "i8" else 10  # + 2 row quantisations
+        # LN1, grouped k/v/r, WKV, att out, LN2, ffn receptance, ffn key,
+        # ffn value (+ 2 row quantisations for w8a8)
+        per_layer = 10 if m.spec.wdtype == "i8" else 8
         per_window = 1 + per_layer * L + 2 + 2   # embed, layers, ln_out+head, cdf+encode
         return 2 + self.windows * per_window + 1
 
@@ -348,7 +350,7 @@ class DecompressPlan:
         m = self.codec.model
         if self.fused:
             return 2 + self.Tmax * 3  # fused layers, head, decode
-        per_layer = 12 if m.spec.wdtype == "i8" else 10
+        per_layer = 10 if m.spec.wdtype == "i8" else 8
         return 2 + self.Tmax * (1 + per_layer * m.spec.n_layer + 2 + 1)
 
     def fetch(self) -> list[np.ndarray]:
